@@ -1,0 +1,196 @@
+/*
+ * zonos2_cuda.h -- C ABI of the B200 (sm_100a) per-decode-step output path of
+ * zonos2.cpp: the 9-codebook output head (hidden 2048 -> 9 x 1024 logits), the
+ * tanh softcap 15*tanh(x/15) and the sampler (repetition penalty, temperature,
+ * top-k / top-p / min-p, token masks, seeded categorical draw).
+ *
+ * Conventions
+ *   - Every entry point returns int: >= 0 on success (a token id where the
+ *     reference returned one), a negative ZONOS2CU_E* code on failure.  No C++
+ *     exception crosses this boundary.
+ *   - "_dev" pointers are CUDA device pointers owned by the caller; calls that
+ *     take them are asynchronous and ordered on the cudaStream_t passed as
+ *     `stream` (NULL = the legacy default stream).  "_host" pointers are host
+ *     memory; those calls copy in and out and return when the result is on the
+ *     host.
+ *   - The library allocates device memory only inside zonos2cu_ctx_create /
+ *     zonos2cu_set_head (owned by the context) and on the first call of
+ *     zonos2cu_sample_token on a device (a small per-device staging area).
+ *   - A context belongs to one device and is not thread-safe; use one per
+ *     (device, host thread).
+ *
+ * Reference interfaces replaced (paths relative to the zonos2.cpp tree):
+ *   sample_token(Xoshiro256&, const float*, int, float, int, float, float)
+ *                                         src/zonos2_generate.cpp:36-93
+ *   Xoshiro256 seeding / next / randf     src/zonos2_generate.cpp:11-33
+ *   head: linear_forward(multi_output)    src/zonos2_model.cpp:200-216, :687-690
+ *   softcap + [n_tok, 9, audio_vocab]     src/zonos2_model.cpp:692-703
+ *   the per-step sampling loop            src/zonos2_generate.cpp:259-267
+ */
+#ifndef ZONOS2_CUDA_H
+#define ZONOS2_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes --------------------------------------------------------- */
+#define ZONOS2CU_OK 0
+#define ZONOS2CU_EINVAL (-1)       /* an argument is out of range or NULL          */
+#define ZONOS2CU_ECUDA (-2)        /* a CUDA runtime / driver call failed          */
+#define ZONOS2CU_ENOMEM (-3)       /* a device allocation failed                   */
+#define ZONOS2CU_ESTATE (-4)       /* context not ready (e.g. no head weights set) */
+#define ZONOS2CU_EUNSUPPORTED (-5) /* shape outside what the kernels implement     */
+#define ZONOS2CU_EDEVICE (-6)      /* a kernel reported a bounded wait that expired */
+
+/* ---- per-row flags written next to each sampled code ---------------------- */
+#define ZONOS2CU_FLAG_ALL_MASKED 1 /* no logit >= -1e9 survived: code = pad_id     */
+#define ZONOS2CU_FLAG_NONFINITE 2  /* a NaN / +inf logit was treated as masked     */
+
+typedef enum { ZONOS2CU_F32 = 0, ZONOS2CU_BF16 = 1 } zonos2cu_dtype;
+
+/* Sampler knobs.  Meaning and defaults follow Zonos2GenParams
+ * (src/zonos2.h:244-254).  repetition_penalty is build-defined (the reference
+ * declares it but never reads it): every distinct token of the row's history
+ * window is scaled once, l > 0 ? l * RN(1/rho) : l * rho; 1.0 disables it.
+ * pad_id is the code forced by the delay-pattern mask and returned for
+ * all-masked rows. */
+typedef struct {
+    float temperature; /* > 0                                    default 0.7  */
+    int top_k;         /* <= 0 or >= vocab: off                  default 50   */
+    float top_p;       /* >= 1: off                              default 0.9  */
+    float min_p;       /* in [0, 1]; 0: off                      default 0.02 */
+    float repetition_penalty; /* > 0; 1: off                     default 1.0  */
+    int pad_id;        /* in [0, vocab)                          default 1023 */
+} zonos2cu_sample_params;
+
+/* Fills *p with the defaults above. */
+void zonos2cu_default_params(zonos2cu_sample_params *p);
+
+/* Library version string and the last CUDA error text seen on this thread. */
+const char *zonos2cu_version(void);
+const char *zonos2cu_last_error(void);
+
+/* ---- generator ------------------------------------------------------------ */
+
+/* Xoshiro256** seeded as the reference does (src/zonos2_generate.cpp:13-19):
+ * state[i] = seed ^ K_i, then 20 discarded outputs.  Host-side helper. */
+void zonos2cu_rng_seed(uint64_t seed, uint64_t state[4]);
+
+/* ---- the drop-in for sample_token (src/zonos2_generate.cpp:36-37) --------- */
+
+/* Same arguments and result as the reference's
+ *   static int sample_token(Xoshiro256& rng, const float* logits,
+ *                           int vocab_size, float temp, int top_k,
+ *                           float top_p, float min_p);
+ * rng_state are the generator's four state words (host memory), advanced by
+ * exactly one draw; logits are vocab_size host floats (1 <= vocab_size <=
+ * 1024).  The row is sampled on the current CUDA device.  Equal
+ * probabilities are taken in ascending token order.  Returns the token id,
+ * or a negative ZONOS2CU_E* code (temp <= 0, NaN knobs, min_p > 1, or an
+ * all-masked row -- the cases where the reference is undefined). */
+int zonos2cu_sample_token(uint64_t rng_state[4], const float *logits, int vocab_size,
+                          float temp, int top_k, float top_p, float min_p);
+
+/* ---- stateless batched sampler (device pointers) -------------------------- */
+
+/* One decode step over n_streams x n_cb rows.  Row (s, c) is
+ * logits_dev[(s*n_cb + c) * row_stride .. + vocab) (row_stride >= vocab; the
+ * reference's [n_tok, 9, 1026] layout is row_stride = 1026).
+ *   rng_dev      [n_streams][4] u64: stream s draws one uniform per codebook,
+ *                in codebook order (the reference's order at
+ *                src/zonos2_generate.cpp:259-267), and is advanced by n_cb.
+ *   hist_dev     [n_streams][n_cb][hist_len] i32 ring (may be NULL when
+ *                hist_len == 0): read for the repetition penalty, then the
+ *                sampled code is written at hist_pos.  Entries outside
+ *                [0, vocab) are ignored (use -1 for empty slots).
+ *   allow_dev    [n_streams][ceil(vocab/32)] u32 or NULL: bit t of stream s
+ *                clear masks token t for all its codebooks.
+ *   delay_step   >= 0: codebook c with delay_step < c may only emit pad_id
+ *                (the delay pattern); < 0: off.
+ *   codes_dev    [n_streams][n_cb] i32 output; flags_dev the same or NULL.
+ * Limits: 1 <= vocab <= 1024, 1 <= n_cb <= 16. */
+int zonos2cu_sample_rows(const float *logits_dev, int n_streams, int n_cb, int vocab,
+                         long long row_stride, const zonos2cu_sample_params *params,
+                         uint64_t *rng_dev, int32_t *hist_dev, int hist_len, int hist_pos,
+                         const uint32_t *allow_dev, int delay_step, int32_t *codes_dev,
+                         int32_t *flags_dev, void *stream);
+
+/* ---- stateless output head + softcap (device pointers) -------------------- */
+
+/* logits_dev[b][c][v] = softcap * tanh(dot(hidden[b], W[c*rows_per_cb + v]) / softcap)
+ * for b < batch, c < n_cb, v < vocab (softcap <= 0: no cap).  W_dev is the
+ * head weight [n_cb*rows_per_cb][dim] row-major -- the reference's
+ * multi_output / output.bin layout is rows_per_cb = 1026, vocab = 1024
+ * (src/zonos2_loader.cpp:133-136) -- and hidden_dev is [batch][dim], both of
+ * `dtype`.  F32 runs an f32-exact GEMV (f64 accumulation); BF16 runs the
+ * tcgen05 tensor-core GEMM (f32 accumulation in TMEM) and needs
+ * dim % 64 == 0, vocab % 64 == 0 and 16-byte aligned rows. */
+int zonos2cu_head_softcap(const void *W_dev, zonos2cu_dtype dtype, int rows_per_cb, int n_cb,
+                          int vocab, int dim, const void *hidden_dev, int batch, float softcap,
+                          float *logits_dev, void *stream);
+
+/* ---- context: device-resident state for a batch of decode streams --------- */
+
+typedef struct zonos2cu_ctx zonos2cu_ctx;
+
+typedef struct {
+    int n_streams;   /* decode streams held by this context (this device's shard) */
+    int n_cb;        /* codebooks per frame: 9                                     */
+    int vocab;       /* sampled tokens per codebook: 1024                          */
+    int dim;         /* hidden size for the fused head: 2048 (0: sampler only)     */
+    int hist_len;    /* repetition-history window per row (0: none)                */
+    uint64_t seed;   /* stream s uses Xoshiro256(seed + first_stream + s)          */
+    uint64_t first_stream; /* global index of this shard's first stream           */
+} zonos2cu_dims;
+
+int zonos2cu_ctx_create(int device, const zonos2cu_dims *dims, zonos2cu_ctx **out);
+int zonos2cu_ctx_destroy(zonos2cu_ctx *ctx);
+
+/* Head weights from host memory, [n_cb*rows_per_cb][dim] of dtype
+ * (rows_per_cb = 1026 for the reference's output.bin; only the first vocab
+ * rows of each codebook are kept on the device). */
+int zonos2cu_set_head(zonos2cu_ctx *ctx, const void *W_host, zonos2cu_dtype dtype,
+                      int rows_per_cb);
+/* History ring [n_streams][n_cb][hist_len] and its write position. */
+int zonos2cu_set_history(zonos2cu_ctx *ctx, const int32_t *hist_host, int hist_pos);
+int zonos2cu_get_history(zonos2cu_ctx *ctx, int32_t *hist_host, int *hist_pos);
+/* Generator states [n_streams][4]. */
+int zonos2cu_set_rng(zonos2cu_ctx *ctx, const uint64_t *state_host);
+int zonos2cu_get_rng(zonos2cu_ctx *ctx, uint64_t *state_host);
+/* Allow bitmask [n_streams][ceil(vocab/32)]; NULL clears it. */
+int zonos2cu_set_allow(zonos2cu_ctx *ctx, const uint32_t *bits_host);
+
+/* One sampling step from device logits [n_streams][n_cb][row_stride]; the
+ * history position advances by one (mod hist_len) on success. */
+int zonos2cu_ctx_sample(zonos2cu_ctx *ctx, const float *logits_dev, long long row_stride,
+                        const zonos2cu_sample_params *params, int delay_step,
+                        int32_t *codes_dev, int32_t *flags_dev, void *stream);
+/* The same from host logits [n_streams][n_cb][row_stride] to host codes/flags
+ * (flags may be NULL): copies in, samples, copies out, returns when done. */
+int zonos2cu_ctx_sample_host(zonos2cu_ctx *ctx, const float *logits_host, long long row_stride,
+                             const zonos2cu_sample_params *params, int delay_step,
+                             int32_t *codes_host, int32_t *flags_host);
+/* One fused step: hidden [n_streams][dim] (device, dtype) -> head + softcap ->
+ * sampler.  logits_out_dev ([n_streams][n_cb][vocab] f32) may be NULL. */
+int zonos2cu_ctx_step(zonos2cu_ctx *ctx, const void *hidden_dev, zonos2cu_dtype dtype,
+                      const zonos2cu_sample_params *params, int delay_step, int32_t *codes_dev,
+                      int32_t *flags_dev, float *logits_out_dev, void *stream);
+/* The same from host hidden states to host codes. */
+int zonos2cu_ctx_step_host(zonos2cu_ctx *ctx, const void *hidden_host, zonos2cu_dtype dtype,
+                           const zonos2cu_sample_params *params, int delay_step,
+                           int32_t *codes_host, int32_t *flags_host);
+/* The context's CUDA stream (cudaStream_t), for callers that order work on it. */
+void *zonos2cu_ctx_stream(zonos2cu_ctx *ctx);
+
+/* Reads and clears the device-side error word that bounded waits set when
+ * they expire (synchronises the current device).  0 = no error. */
+int zonos2cu_device_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ZONOS2_CUDA_H */

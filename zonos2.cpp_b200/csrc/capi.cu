@@ -1,0 +1,541 @@
+// capi.cu -- the extern "C" boundary declared in include/zonos2_cuda.h.
+//
+// Host-side argument checks, the per-device staging of the sample_token
+// drop-in, and the context that keeps a shard of decode streams' generator
+// states, history rings and masks resident in HBM.
+#include <math.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+#include <new>
+
+#include "common.cuh"
+#include "head.cuh"
+#include "sampler.cuh"
+#include "zonos2_cuda.h"
+
+namespace {
+
+thread_local char tl_error[256] = "";
+
+int cuda_fail(cudaError_t e, const char *what)
+{
+    snprintf(tl_error, sizeof(tl_error), "%s: %s", what, cudaGetErrorString(e));
+    return e == cudaErrorMemoryAllocation ? ZONOS2CU_ENOMEM : ZONOS2CU_ECUDA;
+}
+
+#define Z2_CK(call)                                               \
+    do {                                                          \
+        const cudaError_t e_ = (call);                            \
+        if (e_ != cudaSuccess) return cuda_fail(e_, #call);       \
+    } while (0)
+
+int check_params(const zonos2cu_sample_params *p, int vocab)
+{
+    if (!p) return ZONOS2CU_EINVAL;
+    if (!(p->temperature > 0.0f) || !isfinite(p->temperature)) return ZONOS2CU_EINVAL;
+    if (isnan(p->top_p)) return ZONOS2CU_EINVAL;
+    // min_p > 1 empties the candidate list: undefined in the reference
+    if (isnan(p->min_p) || p->min_p > 1.0f) return ZONOS2CU_EINVAL;
+    if (!(p->repetition_penalty > 0.0f) || !isfinite(p->repetition_penalty))
+        return ZONOS2CU_EINVAL;
+    if (p->pad_id < 0 || p->pad_id >= vocab) return ZONOS2CU_EINVAL;
+    return ZONOS2CU_OK;
+}
+
+void fill_sample_args(z2::SampleArgs &a, const zonos2cu_sample_params *p)
+{
+    a.temperature = p->temperature;
+    a.top_k = p->top_k;
+    a.top_p = p->top_p;
+    a.min_p = p->min_p;
+    a.rho = p->repetition_penalty;
+    a.inv_rho = 1.0f / p->repetition_penalty;
+    a.pad_id = p->pad_id;
+}
+
+int check_rows(const float *logits, int n_streams, int n_cb, int vocab, long long row_stride,
+               uint64_t *rng, int32_t *hist, int hist_len, int hist_pos, int32_t *codes)
+{
+    if (n_streams < 0 || n_cb < 1 || n_cb > z2::kSamplerCbMax) return ZONOS2CU_EINVAL;
+    if (vocab < 1) return ZONOS2CU_EINVAL;
+    if (vocab > z2::kSamplerVocabMax) return ZONOS2CU_EUNSUPPORTED;
+    if (row_stride < vocab) return ZONOS2CU_EINVAL;
+    if (hist_len < 0) return ZONOS2CU_EINVAL;
+    if (hist_len > 0 && (!hist || hist_pos < 0 || hist_pos >= hist_len)) return ZONOS2CU_EINVAL;
+    if (n_streams > 0 && (!logits || !rng || !codes)) return ZONOS2CU_EINVAL;
+    return ZONOS2CU_OK;
+}
+
+int launch_rows(const float *logits, int n_streams, int n_cb, int vocab, long long row_stride,
+                const zonos2cu_sample_params *params, uint64_t *rng, int32_t *hist,
+                int hist_len, int hist_pos, const uint32_t *allow, int delay_step,
+                int32_t *codes, int32_t *flags, cudaStream_t stream)
+{
+    z2::SampleArgs a{};
+    a.logits = logits;
+    a.row_stride = row_stride;
+    a.n_streams = n_streams;
+    a.n_cb = n_cb;
+    a.vocab = vocab;
+    fill_sample_args(a, params);
+    a.rng = rng;
+    a.hist = hist_len > 0 ? hist : nullptr;
+    a.hist_len = hist_len;
+    a.hist_pos = hist_pos;
+    a.allow = allow;
+    a.allow_words = (vocab + 31) / 32;
+    a.delay_step = delay_step;
+    a.codes = codes;
+    a.flags = flags;
+    a.vec_logits = (row_stride % 4 == 0) && (vocab % 4 == 0) && ((uintptr_t)logits % 16 == 0);
+    a.vec_hist = hist_len > 0 && (hist_len % 4 == 0) && ((uintptr_t)hist % 16 == 0);
+    Z2_CK(z2::launch_sample(a, stream));
+    return ZONOS2CU_OK;
+}
+
+// ---- per-device staging for the sample_token drop-in --------------------
+struct Staging {
+    std::mutex mu;
+    bool ready = false;
+    cudaStream_t stream = nullptr;
+    float *logits = nullptr;    // [1024]
+    uint64_t *rng = nullptr;    // [4]
+    int32_t *out = nullptr;     // [2] code, flag
+};
+Staging g_staging[64];
+
+}  // namespace
+
+extern "C" {
+
+void zonos2cu_default_params(zonos2cu_sample_params *p)
+{
+    if (!p) return;
+    p->temperature = 0.7f;
+    p->top_k = 50;
+    p->top_p = 0.9f;
+    p->min_p = 0.02f;
+    p->repetition_penalty = 1.0f;
+    p->pad_id = 1023;
+}
+
+const char *zonos2cu_version(void) { return "zonos2cu 0.1 (sm_100a)"; }
+
+const char *zonos2cu_last_error(void) { return tl_error; }
+
+void zonos2cu_rng_seed(uint64_t seed, uint64_t state[4])
+{
+    // src/zonos2_generate.cpp:13-19
+    uint64_t s0 = seed ^ 0x9E3779B97F4A7C15ULL, s1 = seed ^ 0xBF58476D1CE4E5B9ULL,
+             s2 = seed ^ 0x94D049BB133111EBULL, s3 = seed ^ 0x3243F6A8885A308DULL;
+    for (int i = 0; i < 20; i++) {
+        const uint64_t t = s1 << 17;
+        s2 ^= s0;
+        s3 ^= s1;
+        s1 ^= s2;
+        s0 ^= s3;
+        s2 ^= t;
+        s3 = (s3 << 45) | (s3 >> 19);
+    }
+    state[0] = s0;
+    state[1] = s1;
+    state[2] = s2;
+    state[3] = s3;
+}
+
+int zonos2cu_sample_rows(const float *logits_dev, int n_streams, int n_cb, int vocab,
+                         long long row_stride, const zonos2cu_sample_params *params,
+                         uint64_t *rng_dev, int32_t *hist_dev, int hist_len, int hist_pos,
+                         const uint32_t *allow_dev, int delay_step, int32_t *codes_dev,
+                         int32_t *flags_dev, void *stream)
+{
+    int rc = check_rows(logits_dev, n_streams, n_cb, vocab, row_stride, rng_dev, hist_dev,
+                        hist_len, hist_pos, codes_dev);
+    if (rc) return rc;
+    if ((rc = check_params(params, vocab))) return rc;
+    return launch_rows(logits_dev, n_streams, n_cb, vocab, row_stride, params, rng_dev, hist_dev,
+                       hist_len, hist_pos, allow_dev, delay_step, codes_dev, flags_dev,
+                       (cudaStream_t)stream);
+}
+
+int zonos2cu_sample_token(uint64_t rng_state[4], const float *logits, int vocab_size,
+                          float temp, int top_k, float top_p, float min_p)
+{
+    if (!rng_state || !logits || vocab_size < 1) return ZONOS2CU_EINVAL;
+    if (vocab_size > z2::kSamplerVocabMax) return ZONOS2CU_EUNSUPPORTED;
+    zonos2cu_sample_params p;
+    p.temperature = temp;
+    p.top_k = top_k;
+    p.top_p = top_p;
+    p.min_p = min_p;
+    p.repetition_penalty = 1.0f;
+    p.pad_id = 0;
+    int rc = check_params(&p, vocab_size);
+    if (rc) return rc;
+    int dev = 0;
+    Z2_CK(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return ZONOS2CU_EINVAL;
+    Staging &st = g_staging[dev];
+    std::lock_guard<std::mutex> lock(st.mu);
+    if (!st.ready) {
+        // first call on this device: a small staging area, kept until exit
+        Z2_CK(cudaStreamCreateWithFlags(&st.stream, cudaStreamNonBlocking));
+        Z2_CK(cudaMalloc(&st.logits, sizeof(float) * z2::kSamplerVocabMax));
+        Z2_CK(cudaMalloc(&st.rng, sizeof(uint64_t) * 4));
+        Z2_CK(cudaMalloc(&st.out, sizeof(int32_t) * 2));
+        st.ready = true;
+    }
+    Z2_CK(cudaMemcpyAsync(st.logits, logits, sizeof(float) * vocab_size, cudaMemcpyHostToDevice,
+                          st.stream));
+    Z2_CK(cudaMemcpyAsync(st.rng, rng_state, sizeof(uint64_t) * 4, cudaMemcpyHostToDevice,
+                          st.stream));
+    rc = launch_rows(st.logits, 1, 1, vocab_size, vocab_size, &p, st.rng, nullptr, 0, 0, nullptr,
+                     -1, st.out, st.out + 1, st.stream);
+    if (rc) return rc;
+    int32_t out[2];
+    uint64_t rs[4];
+    Z2_CK(cudaMemcpyAsync(out, st.out, sizeof(out), cudaMemcpyDeviceToHost, st.stream));
+    Z2_CK(cudaMemcpyAsync(rs, st.rng, sizeof(rs), cudaMemcpyDeviceToHost, st.stream));
+    Z2_CK(cudaStreamSynchronize(st.stream));
+    memcpy(rng_state, rs, sizeof(rs));
+    if (out[1] & ZONOS2CU_FLAG_ALL_MASKED) return ZONOS2CU_EINVAL;
+    return out[0];
+}
+
+int zonos2cu_head_softcap(const void *W_dev, zonos2cu_dtype dtype, int rows_per_cb, int n_cb,
+                          int vocab, int dim, const void *hidden_dev, int batch, float softcap,
+                          float *logits_dev, void *stream)
+{
+    if (n_cb < 1 || vocab < 1 || dim < 1 || batch < 0 || rows_per_cb < vocab)
+        return ZONOS2CU_EINVAL;
+    if (isnan(softcap)) return ZONOS2CU_EINVAL;
+    if (batch > 0 && (!W_dev || !hidden_dev || !logits_dev)) return ZONOS2CU_EINVAL;
+    z2::HeadArgs a{W_dev, rows_per_cb, n_cb, vocab, dim, hidden_dev, batch, softcap, logits_dev};
+    cudaError_t e;
+    if (dtype == ZONOS2CU_F32) {
+        e = z2::launch_head_gemv_f32(a, (cudaStream_t)stream);
+    } else if (dtype == ZONOS2CU_BF16) {
+        e = z2::launch_head_tc_bf16(a, (cudaStream_t)stream);
+        if (e == cudaErrorNotSupported) return ZONOS2CU_EUNSUPPORTED;
+    } else {
+        return ZONOS2CU_EINVAL;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "head launch");
+    return ZONOS2CU_OK;
+}
+
+int zonos2cu_device_error(void)
+{
+    Z2_CK(cudaDeviceSynchronize());
+    int v = 0;
+    const int e = z2::read_and_clear_device_error(&v);
+    if (e) return cuda_fail((cudaError_t)e, "device error word");
+    return v;
+}
+
+}  // extern "C"
+
+// ---- context --------------------------------------------------------------
+
+struct zonos2cu_ctx {
+    int device = 0;
+    zonos2cu_dims dims{};
+    cudaStream_t stream = nullptr;
+    uint64_t *rng = nullptr;     // [S][4]
+    int32_t *hist = nullptr;     // [S][C][H]
+    int hist_pos = 0;
+    uint32_t *allow = nullptr;   // [S][words]
+    bool allow_on = false;
+    void *head = nullptr;        // [C*V][D] of head_dtype
+    zonos2cu_dtype head_dtype = ZONOS2CU_F32;
+    float *logits = nullptr;     // [S][C][V] fused-step intermediate
+    // host-path staging, grown on demand
+    float *in_logits = nullptr;
+    size_t in_logits_bytes = 0;
+    void *in_hidden = nullptr;
+    size_t in_hidden_bytes = 0;
+    int32_t *out = nullptr;      // [2][S][C] codes, flags
+};
+
+namespace {
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev)
+    {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard()
+    {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+size_t n_rows(const zonos2cu_ctx *c) { return (size_t)c->dims.n_streams * c->dims.n_cb; }
+
+int grow(void **p, size_t *cap, size_t want)
+{
+    if (*cap >= want) return ZONOS2CU_OK;
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+    *cap = 0;
+    Z2_CK(cudaMalloc(p, want));
+    *cap = want;
+    return ZONOS2CU_OK;
+}
+
+int ensure_out(zonos2cu_ctx *c)
+{
+    if (c->out) return ZONOS2CU_OK;
+    Z2_CK(cudaMalloc(&c->out, sizeof(int32_t) * 2 * (n_rows(c) ? n_rows(c) : 1)));
+    return ZONOS2CU_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int zonos2cu_ctx_create(int device, const zonos2cu_dims *d, zonos2cu_ctx **out)
+{
+    if (!d || !out) return ZONOS2CU_EINVAL;
+    *out = nullptr;
+    if (d->n_streams < 0 || d->n_cb < 1 || d->n_cb > z2::kSamplerCbMax || d->vocab < 1 ||
+        d->dim < 0 || d->hist_len < 0)
+        return ZONOS2CU_EINVAL;
+    if (d->vocab > z2::kSamplerVocabMax) return ZONOS2CU_EUNSUPPORTED;
+    int ndev = 0;
+    Z2_CK(cudaGetDeviceCount(&ndev));
+    if (device < 0 || device >= ndev) return ZONOS2CU_EINVAL;
+    DeviceGuard g(device);
+    zonos2cu_ctx *c = new (std::nothrow) zonos2cu_ctx();
+    if (!c) return ZONOS2CU_ENOMEM;
+    c->device = device;
+    c->dims = *d;
+    int rc = ZONOS2CU_OK;
+    do {
+        cudaError_t e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+        if (e != cudaSuccess) { rc = cuda_fail(e, "stream"); break; }
+        const size_t S = (size_t)d->n_streams;
+        if (S == 0) break;
+        e = cudaMalloc(&c->rng, sizeof(uint64_t) * 4 * S);
+        if (e != cudaSuccess) { rc = cuda_fail(e, "rng"); break; }
+        uint64_t *h = new (std::nothrow) uint64_t[4 * S];
+        if (!h) { rc = ZONOS2CU_ENOMEM; break; }
+        for (size_t s = 0; s < S; s++) zonos2cu_rng_seed(d->seed + d->first_stream + s, h + 4 * s);
+        e = cudaMemcpy(c->rng, h, sizeof(uint64_t) * 4 * S, cudaMemcpyHostToDevice);
+        delete[] h;
+        if (e != cudaSuccess) { rc = cuda_fail(e, "rng upload"); break; }
+        if (d->hist_len > 0) {
+            const size_t hb = sizeof(int32_t) * S * d->n_cb * (size_t)d->hist_len;
+            e = cudaMalloc(&c->hist, hb);
+            if (e == cudaSuccess) e = cudaMemset(c->hist, 0xff, hb);  // -1: empty slots
+            if (e != cudaSuccess) { rc = cuda_fail(e, "history"); break; }
+        }
+    } while (0);
+    if (rc) {
+        zonos2cu_ctx_destroy(c);
+        return rc;
+    }
+    *out = c;
+    return ZONOS2CU_OK;
+}
+
+int zonos2cu_ctx_destroy(zonos2cu_ctx *c)
+{
+    if (!c) return ZONOS2CU_OK;
+    DeviceGuard g(c->device);
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    cudaFree(c->rng);
+    cudaFree(c->hist);
+    cudaFree(c->allow);
+    cudaFree(c->head);
+    cudaFree(c->logits);
+    cudaFree(c->in_logits);
+    cudaFree(c->in_hidden);
+    cudaFree(c->out);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+    return ZONOS2CU_OK;
+}
+
+void *zonos2cu_ctx_stream(zonos2cu_ctx *c) { return c ? (void *)c->stream : nullptr; }
+
+int zonos2cu_set_head(zonos2cu_ctx *c, const void *W_host, zonos2cu_dtype dtype, int rows_per_cb)
+{
+    if (!c || !W_host || c->dims.dim < 1 || rows_per_cb < c->dims.vocab) return ZONOS2CU_EINVAL;
+    if (dtype != ZONOS2CU_F32 && dtype != ZONOS2CU_BF16) return ZONOS2CU_EINVAL;
+    DeviceGuard g(c->device);
+    const size_t es = dtype == ZONOS2CU_F32 ? 4 : 2;
+    const size_t row_bytes = es * (size_t)c->dims.dim;
+    const size_t V = (size_t)c->dims.vocab, C = (size_t)c->dims.n_cb;
+    cudaFree(c->head);
+    c->head = nullptr;
+    Z2_CK(cudaMalloc(&c->head, row_bytes * V * C));
+    // keep the sampled rows of each codebook: one 2-D copy per codebook
+    for (size_t cb = 0; cb < C; cb++) {
+        const char *src = static_cast<const char *>(W_host) + cb * (size_t)rows_per_cb * row_bytes;
+        Z2_CK(cudaMemcpy(static_cast<char *>(c->head) + cb * V * row_bytes, src, V * row_bytes,
+                         cudaMemcpyHostToDevice));
+    }
+    c->head_dtype = dtype;
+    if (!c->logits && n_rows(c)) Z2_CK(cudaMalloc(&c->logits, sizeof(float) * n_rows(c) * V));
+    return ZONOS2CU_OK;
+}
+
+int zonos2cu_set_history(zonos2cu_ctx *c, const int32_t *hist_host, int hist_pos)
+{
+    if (!c || !hist_host || c->dims.hist_len < 1) return ZONOS2CU_EINVAL;
+    if (hist_pos < 0 || hist_pos >= c->dims.hist_len) return ZONOS2CU_EINVAL;
+    DeviceGuard g(c->device);
+    if (n_rows(c))
+        Z2_CK(cudaMemcpy(c->hist, hist_host, sizeof(int32_t) * n_rows(c) * c->dims.hist_len,
+                         cudaMemcpyHostToDevice));
+    c->hist_pos = hist_pos;
+    return ZONOS2CU_OK;
+}
+
+int zonos2cu_get_history(zonos2cu_ctx *c, int32_t *hist_host, int *hist_pos)
+{
+    if (!c || c->dims.hist_len < 1) return ZONOS2CU_EINVAL;
+    DeviceGuard g(c->device);
+    Z2_CK(cudaStreamSynchronize(c->stream));
+    if (hist_host && n_rows(c))
+        Z2_CK(cudaMemcpy(hist_host, c->hist, sizeof(int32_t) * n_rows(c) * c->dims.hist_len,
+                         cudaMemcpyDeviceToHost));
+    if (hist_pos) *hist_pos = c->hist_pos;
+    return ZONOS2CU_OK;
+}
+
+int zonos2cu_set_rng(zonos2cu_ctx *c, const uint64_t *state_host)
+{
+    if (!c || !state_host) return ZONOS2CU_EINVAL;
+    DeviceGuard g(c->device);
+    if (c->dims.n_streams)
+        Z2_CK(cudaMemcpy(c->rng, state_host, sizeof(uint64_t) * 4 * c->dims.n_streams,
+                         cudaMemcpyHostToDevice));
+    return ZONOS2CU_OK;
+}
+
+int zonos2cu_get_rng(zonos2cu_ctx *c, uint64_t *state_host)
+{
+    if (!c || !state_host) return ZONOS2CU_EINVAL;
+    DeviceGuard g(c->device);
+    Z2_CK(cudaStreamSynchronize(c->stream));
+    if (c->dims.n_streams)
+        Z2_CK(cudaMemcpy(state_host, c->rng, sizeof(uint64_t) * 4 * c->dims.n_streams,
+                         cudaMemcpyDeviceToHost));
+    return ZONOS2CU_OK;
+}
+
+int zonos2cu_set_allow(zonos2cu_ctx *c, const uint32_t *bits_host)
+{
+    if (!c) return ZONOS2CU_EINVAL;
+    DeviceGuard g(c->device);
+    if (!bits_host) {
+        c->allow_on = false;
+        return ZONOS2CU_OK;
+    }
+    const size_t words = (size_t)(c->dims.vocab + 31) / 32 * c->dims.n_streams;
+    if (!c->allow && words) Z2_CK(cudaMalloc(&c->allow, sizeof(uint32_t) * words));
+    if (words)
+        Z2_CK(cudaMemcpy(c->allow, bits_host, sizeof(uint32_t) * words, cudaMemcpyHostToDevice));
+    c->allow_on = true;
+    return ZONOS2CU_OK;
+}
+
+int zonos2cu_ctx_sample(zonos2cu_ctx *c, const float *logits_dev, long long row_stride,
+                        const zonos2cu_sample_params *params, int delay_step, int32_t *codes_dev,
+                        int32_t *flags_dev, void *stream)
+{
+    if (!c) return ZONOS2CU_EINVAL;
+    DeviceGuard g(c->device);
+    const zonos2cu_dims &d = c->dims;
+    int rc = check_rows(logits_dev, d.n_streams, d.n_cb, d.vocab, row_stride, c->rng, c->hist,
+                        d.hist_len, c->hist_pos, codes_dev);
+    if (rc) return rc;
+    if ((rc = check_params(params, d.vocab))) return rc;
+    rc = launch_rows(logits_dev, d.n_streams, d.n_cb, d.vocab, row_stride, params, c->rng,
+                     c->hist, d.hist_len, c->hist_pos, c->allow_on ? c->allow : nullptr,
+                     delay_step, codes_dev, flags_dev,
+                     stream ? (cudaStream_t)stream : c->stream);
+    if (rc) return rc;
+    if (d.hist_len > 0) c->hist_pos = (c->hist_pos + 1) % d.hist_len;
+    return ZONOS2CU_OK;
+}
+
+int zonos2cu_ctx_sample_host(zonos2cu_ctx *c, const float *logits_host, long long row_stride,
+                             const zonos2cu_sample_params *params, int delay_step,
+                             int32_t *codes_host, int32_t *flags_host)
+{
+    if (!c || !logits_host || !codes_host) return ZONOS2CU_EINVAL;
+    DeviceGuard g(c->device);
+    const size_t rows = n_rows(c);
+    if (row_stride < c->dims.vocab) return ZONOS2CU_EINVAL;
+    int rc = check_params(params, c->dims.vocab);
+    if (rc) return rc;
+    if (rows == 0) return ZONOS2CU_OK;
+    const size_t bytes = sizeof(float) * rows * (size_t)row_stride;
+    if ((rc = grow((void **)&c->in_logits, &c->in_logits_bytes, bytes))) return rc;
+    if ((rc = ensure_out(c))) return rc;
+    Z2_CK(cudaMemcpyAsync(c->in_logits, logits_host, bytes, cudaMemcpyHostToDevice, c->stream));
+    rc = zonos2cu_ctx_sample(c, c->in_logits, row_stride, params, delay_step, c->out,
+                             c->out + rows, c->stream);
+    if (rc) return rc;
+    Z2_CK(cudaMemcpyAsync(codes_host, c->out, sizeof(int32_t) * rows, cudaMemcpyDeviceToHost,
+                          c->stream));
+    if (flags_host)
+        Z2_CK(cudaMemcpyAsync(flags_host, c->out + rows, sizeof(int32_t) * rows,
+                              cudaMemcpyDeviceToHost, c->stream));
+    Z2_CK(cudaStreamSynchronize(c->stream));
+    return ZONOS2CU_OK;
+}
+
+int zonos2cu_ctx_step(zonos2cu_ctx *c, const void *hidden_dev, zonos2cu_dtype dtype,
+                      const zonos2cu_sample_params *params, int delay_step, int32_t *codes_dev,
+                      int32_t *flags_dev, float *logits_out_dev, void *stream)
+{
+    if (!c || !hidden_dev) return ZONOS2CU_EINVAL;
+    if (!c->head) return ZONOS2CU_ESTATE;
+    if (dtype != c->head_dtype) return ZONOS2CU_EINVAL;
+    DeviceGuard g(c->device);
+    const zonos2cu_dims &d = c->dims;
+    int rc = check_params(params, d.vocab);
+    if (rc) return rc;
+    cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+    float *lg = logits_out_dev ? logits_out_dev : c->logits;
+    rc = zonos2cu_head_softcap(c->head, dtype, d.vocab, d.n_cb, d.vocab, d.dim, hidden_dev,
+                               d.n_streams, 15.0f, lg, st);
+    if (rc) return rc;
+    return zonos2cu_ctx_sample(c, lg, d.vocab, params, delay_step, codes_dev, flags_dev, st);
+}
+
+int zonos2cu_ctx_step_host(zonos2cu_ctx *c, const void *hidden_host, zonos2cu_dtype dtype,
+                           const zonos2cu_sample_params *params, int delay_step,
+                           int32_t *codes_host, int32_t *flags_host)
+{
+    if (!c || !hidden_host || !codes_host) return ZONOS2CU_EINVAL;
+    if (!c->head) return ZONOS2CU_ESTATE;
+    DeviceGuard g(c->device);
+    const size_t rows = n_rows(c);
+    if (rows == 0) return ZONOS2CU_OK;
+    const size_t bytes = (dtype == ZONOS2CU_F32 ? 4 : 2) * (size_t)c->dims.n_streams * c->dims.dim;
+    int rc = grow(&c->in_hidden, &c->in_hidden_bytes, bytes);
+    if (rc) return rc;
+    if ((rc = ensure_out(c))) return rc;
+    Z2_CK(cudaMemcpyAsync(c->in_hidden, hidden_host, bytes, cudaMemcpyHostToDevice, c->stream));
+    rc = zonos2cu_ctx_step(c, c->in_hidden, dtype, params, delay_step, c->out, c->out + rows,
+                           nullptr, c->stream);
+    if (rc) return rc;
+    Z2_CK(cudaMemcpyAsync(codes_host, c->out, sizeof(int32_t) * rows, cudaMemcpyDeviceToHost,
+                          c->stream));
+    if (flags_host)
+        Z2_CK(cudaMemcpyAsync(flags_host, c->out + rows, sizeof(int32_t) * rows,
+                              cudaMemcpyDeviceToHost, c->stream));
+    Z2_CK(cudaStreamSynchronize(c->stream));
+    return ZONOS2CU_OK;
+}
+
+}  // extern "C"

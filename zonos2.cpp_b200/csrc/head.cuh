@@ -1,0 +1,31 @@
+// head.cuh -- launcher interface of the output-head kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace z2 {
+
+struct HeadArgs {
+    const void *W;        // [n_cb*rows_per_cb][dim] row-major
+    int rows_per_cb, n_cb, vocab, dim;
+    const void *hidden;   // [batch][dim]
+    int batch;
+    float softcap;        // <= 0: no cap
+    float *out;           // [batch][n_cb][vocab] f32
+};
+
+// f32 weights and hidden states: one warp per output row, f64 accumulation
+// (head_gemv.cu).
+cudaError_t launch_head_gemv_f32(const HeadArgs &a, cudaStream_t stream);
+
+// bf16 weights and hidden states: tcgen05 tensor-core GEMM with the softcap in
+// the TMEM epilogue (head_tc.cu).  Returns cudaErrorNotSupported for shapes it
+// does not implement.
+cudaError_t launch_head_tc_bf16(const HeadArgs &a, cudaStream_t stream);
+
+// Reads and clears the device error word written by the tcgen05 kernel's
+// bounded waits (head_tc.cu).
+int read_and_clear_device_error(int *value);
+
+}  // namespace z2

@@ -1,0 +1,291 @@
+"""Python mirror of zonos2.cpp's decode-step output path over the CUDA library.
+
+Thin ctypes bindings to ``libzonos2cu.so`` (the C ABI in
+``include/zonos2_cuda.h``).  The names follow the reference:
+
+* ``Xoshiro256`` -- the generator of src/zonos2_generate.cpp:11-33 (state
+  words in host memory; seeding and stepping match bit for bit);
+* ``sample_token(rng, logits, vocab_size, temp, top_k, top_p, min_p)`` -- the
+  drop-in for src/zonos2_generate.cpp:36-93, sampled on the current GPU;
+* ``sample_rows`` / ``head_softcap`` -- the batched device-pointer entry points;
+* ``Context`` -- device-resident decode state for a shard of streams.
+
+Device buffers are passed as torch CUDA tensors (PyTorch is only the memory
+and stream plumbing here).  There is no CPU fallback: if the library is
+missing or fails to load, every entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from dataclasses import dataclass
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libzonos2cu.so")
+
+OK, EINVAL, ECUDA, ENOMEM, ESTATE, EUNSUPPORTED, EDEVICE = 0, -1, -2, -3, -4, -5, -6
+FLAG_ALL_MASKED, FLAG_NONFINITE = 1, 2
+F32, BF16 = 0, 1
+
+EXPORTS = (
+    "zonos2cu_default_params", "zonos2cu_version", "zonos2cu_last_error", "zonos2cu_rng_seed",
+    "zonos2cu_sample_token", "zonos2cu_sample_rows", "zonos2cu_head_softcap",
+    "zonos2cu_ctx_create", "zonos2cu_ctx_destroy", "zonos2cu_set_head", "zonos2cu_set_history",
+    "zonos2cu_get_history", "zonos2cu_set_rng", "zonos2cu_get_rng", "zonos2cu_set_allow",
+    "zonos2cu_ctx_sample", "zonos2cu_ctx_sample_host", "zonos2cu_ctx_step",
+    "zonos2cu_ctx_step_host", "zonos2cu_ctx_stream", "zonos2cu_device_error",
+)
+
+
+class Zonos2cuError(RuntimeError):
+    def __init__(self, code: int, what: str):
+        names = {EINVAL: "EINVAL", ECUDA: "ECUDA", ENOMEM: "ENOMEM", ESTATE: "ESTATE",
+                 EUNSUPPORTED: "EUNSUPPORTED", EDEVICE: "EDEVICE"}
+        msg = f"{what} failed: {names.get(code, code)}"
+        detail = last_error() if _lib is not None else ""
+        if detail:
+            msg += f" ({detail})"
+        super().__init__(msg)
+        self.code = code
+
+
+class SampleParams(C.Structure):
+    """zonos2cu_sample_params; defaults follow Zonos2GenParams (src/zonos2.h:244-254)."""
+    _fields_ = [("temperature", C.c_float), ("top_k", C.c_int), ("top_p", C.c_float),
+                ("min_p", C.c_float), ("repetition_penalty", C.c_float), ("pad_id", C.c_int)]
+
+    def __init__(self, temperature=0.7, top_k=50, top_p=0.9, min_p=0.02, repetition_penalty=1.0,
+                 pad_id=1023):
+        super().__init__(temperature, top_k, top_p, min_p, repetition_penalty, pad_id)
+
+
+class Dims(C.Structure):
+    _fields_ = [("n_streams", C.c_int), ("n_cb", C.c_int), ("vocab", C.c_int), ("dim", C.c_int),
+                ("hist_len", C.c_int), ("seed", C.c_uint64), ("first_stream", C.c_uint64)]
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """Load libzonos2cu.so (raises if it is missing: there is no fallback)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is missing: run __graft_entry__.build() or make -C "
+                          f"{HERE}")
+    L = C.CDLL(LIB_PATH)
+    vp, i, f, ll, u64p = C.c_void_p, C.c_int, C.c_float, C.c_longlong, C.POINTER(C.c_uint64)
+    sig = {
+        "zonos2cu_default_params": (None, [C.POINTER(SampleParams)]),
+        "zonos2cu_version": (C.c_char_p, []),
+        "zonos2cu_last_error": (C.c_char_p, []),
+        "zonos2cu_rng_seed": (None, [C.c_uint64, u64p]),
+        "zonos2cu_sample_token": (i, [u64p, vp, i, f, i, f, f]),
+        "zonos2cu_sample_rows": (i, [vp, i, i, i, ll, C.POINTER(SampleParams), vp, vp, i, i, vp,
+                                     i, vp, vp, vp]),
+        "zonos2cu_head_softcap": (i, [vp, i, i, i, i, i, vp, i, f, vp, vp]),
+        "zonos2cu_ctx_create": (i, [i, C.POINTER(Dims), C.POINTER(vp)]),
+        "zonos2cu_ctx_destroy": (i, [vp]),
+        "zonos2cu_set_head": (i, [vp, vp, i, i]),
+        "zonos2cu_set_history": (i, [vp, vp, i]),
+        "zonos2cu_get_history": (i, [vp, vp, C.POINTER(i)]),
+        "zonos2cu_set_rng": (i, [vp, vp]),
+        "zonos2cu_get_rng": (i, [vp, vp]),
+        "zonos2cu_set_allow": (i, [vp, vp]),
+        "zonos2cu_ctx_sample": (i, [vp, vp, ll, C.POINTER(SampleParams), i, vp, vp, vp]),
+        "zonos2cu_ctx_sample_host": (i, [vp, vp, ll, C.POINTER(SampleParams), i, vp, vp]),
+        "zonos2cu_ctx_step": (i, [vp, vp, i, C.POINTER(SampleParams), i, vp, vp, vp, vp]),
+        "zonos2cu_ctx_step_host": (i, [vp, vp, i, C.POINTER(SampleParams), i, vp, vp]),
+        "zonos2cu_ctx_stream": (vp, [vp]),
+        "zonos2cu_device_error": (i, []),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def last_error() -> str:
+    s = lib().zonos2cu_last_error()
+    return s.decode() if s else ""
+
+
+def _check(rc: int, what: str) -> int:
+    if rc < 0:
+        raise Zonos2cuError(rc, what)
+    return rc
+
+
+def _ptr(t) -> int | None:
+    """Device (or host) address of a torch tensor / numpy array, None for None."""
+    if t is None:
+        return None
+    if isinstance(t, int):
+        return t
+    if isinstance(t, np.ndarray):
+        return t.ctypes.data
+    return t.data_ptr()
+
+
+def _stream(stream) -> int | None:
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+def default_params() -> SampleParams:
+    p = SampleParams()
+    lib().zonos2cu_default_params(C.byref(p))
+    return p
+
+
+class Xoshiro256:
+    """The reference's generator (src/zonos2_generate.cpp:11-33); ``s`` are its
+    four state words, seeded by the library as the reference seeds them."""
+
+    def __init__(self, seed: int = 42):
+        self.s = np.zeros(4, np.uint64)
+        lib().zonos2cu_rng_seed(C.c_uint64(seed), self.s.ctypes.data_as(C.POINTER(C.c_uint64)))
+
+
+def sample_token(rng: Xoshiro256, logits, vocab_size: int, temp: float, top_k: int,
+                 top_p: float, min_p: float) -> int:
+    """Drop-in for sample_token (src/zonos2_generate.cpp:36-37): one row of host
+    logits sampled on the current GPU; ``rng`` advances by one draw."""
+    row = np.ascontiguousarray(np.asarray(logits, np.float32)[:vocab_size])
+    rc = lib().zonos2cu_sample_token(rng.s.ctypes.data_as(C.POINTER(C.c_uint64)),
+                                     row.ctypes.data, vocab_size, temp, top_k, top_p, min_p)
+    return _check(rc, "zonos2cu_sample_token")
+
+
+def sample_rows(logits, params: SampleParams, rng, codes, *, flags=None, hist=None, hist_pos=0,
+                allow=None, delay_step=-1, n_streams=None, n_cb=None, vocab=None,
+                row_stride=None, stream=None) -> None:
+    """One batched step.  logits: CUDA f32 [S, C, V] (or give the sizes and a
+    row stride); rng: CUDA int64/uint64 [S, 4]; codes/flags: CUDA int32 [S, C];
+    hist: CUDA int32 [S, C, H] or None; allow: CUDA int32/uint32 [S, ceil(V/32)]."""
+    S = logits.shape[0] if n_streams is None else n_streams
+    Cb = logits.shape[1] if n_cb is None else n_cb
+    V = logits.shape[-1] if vocab is None else vocab
+    stride = logits.shape[-1] if row_stride is None else row_stride
+    H = 0 if hist is None else hist.shape[-1]
+    rc = lib().zonos2cu_sample_rows(_ptr(logits), S, Cb, V, stride, C.byref(params), _ptr(rng),
+                                    _ptr(hist), H, hist_pos, _ptr(allow), delay_step, _ptr(codes),
+                                    _ptr(flags), _stream(stream))
+    _check(rc, "zonos2cu_sample_rows")
+
+
+def head_softcap(W, dtype: int, rows_per_cb: int, n_cb: int, vocab: int, hidden, out,
+                 softcap: float = 15.0, stream=None) -> None:
+    """logits[b, c, v] = softcap * tanh(W[c*rows_per_cb + v] . hidden[b] / softcap)."""
+    B, D = hidden.shape
+    rc = lib().zonos2cu_head_softcap(_ptr(W), dtype, rows_per_cb, n_cb, vocab, D, _ptr(hidden), B,
+                                     softcap, _ptr(out), _stream(stream))
+    _check(rc, "zonos2cu_head_softcap")
+
+
+def device_error() -> int:
+    return _check(lib().zonos2cu_device_error(), "zonos2cu_device_error")
+
+
+@dataclass
+class _Shape:
+    n_streams: int
+    n_cb: int
+    vocab: int
+    dim: int
+    hist_len: int
+
+
+class Context:
+    """Device-resident decode state for one shard of streams (zonos2cu_ctx)."""
+
+    def __init__(self, device: int, n_streams: int, n_cb: int = 9, vocab: int = 1024,
+                 dim: int = 0, hist_len: int = 0, seed: int = 42, first_stream: int = 0):
+        d = Dims(n_streams, n_cb, vocab, dim, hist_len, seed, first_stream)
+        h = C.c_void_p()
+        _check(lib().zonos2cu_ctx_create(device, C.byref(d), C.byref(h)), "zonos2cu_ctx_create")
+        self.h = h
+        self.shape = _Shape(n_streams, n_cb, vocab, dim, hist_len)
+
+    def close(self) -> None:
+        if self.h:
+            lib().zonos2cu_ctx_destroy(self.h)
+            self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def stream(self) -> int:
+        return lib().zonos2cu_ctx_stream(self.h)
+
+    def set_head(self, W: np.ndarray, dtype: int, rows_per_cb: int) -> None:
+        W = np.ascontiguousarray(W)
+        _check(lib().zonos2cu_set_head(self.h, W.ctypes.data, dtype, rows_per_cb), "set_head")
+
+    def set_history(self, hist: np.ndarray, hist_pos: int) -> None:
+        hist = np.ascontiguousarray(hist, np.int32)
+        _check(lib().zonos2cu_set_history(self.h, hist.ctypes.data, hist_pos), "set_history")
+
+    def get_history(self):
+        s = self.shape
+        hist = np.zeros((s.n_streams, s.n_cb, s.hist_len), np.int32)
+        pos = C.c_int()
+        _check(lib().zonos2cu_get_history(self.h, hist.ctypes.data, C.byref(pos)), "get_history")
+        return hist, pos.value
+
+    def set_rng(self, st: np.ndarray) -> None:
+        st = np.ascontiguousarray(st, np.uint64)
+        _check(lib().zonos2cu_set_rng(self.h, st.ctypes.data), "set_rng")
+
+    def get_rng(self) -> np.ndarray:
+        st = np.zeros((self.shape.n_streams, 4), np.uint64)
+        _check(lib().zonos2cu_get_rng(self.h, st.ctypes.data), "get_rng")
+        return st
+
+    def set_allow(self, bits) -> None:
+        if bits is None:
+            _check(lib().zonos2cu_set_allow(self.h, None), "set_allow")
+            return
+        bits = np.ascontiguousarray(bits, np.uint32)
+        _check(lib().zonos2cu_set_allow(self.h, bits.ctypes.data), "set_allow")
+
+    def sample(self, logits, params: SampleParams, codes, flags=None, delay_step=-1,
+               row_stride=None, stream=None) -> None:
+        """Device step on ``stream`` (default: torch's current stream)."""
+        stride = logits.shape[-1] if row_stride is None else row_stride
+        rc = lib().zonos2cu_ctx_sample(self.h, _ptr(logits), stride, C.byref(params), delay_step,
+                                       _ptr(codes), _ptr(flags), _stream(stream))
+        _check(rc, "zonos2cu_ctx_sample")
+
+    def sample_host(self, logits: np.ndarray, params: SampleParams, codes: np.ndarray,
+                    flags: np.ndarray | None = None, delay_step=-1, row_stride=None) -> None:
+        stride = logits.shape[-1] if row_stride is None else row_stride
+        rc = lib().zonos2cu_ctx_sample_host(self.h, _ptr(logits), stride, C.byref(params),
+                                            delay_step, _ptr(codes), _ptr(flags))
+        _check(rc, "zonos2cu_ctx_sample_host")
+
+    def step(self, hidden, dtype: int, params: SampleParams, codes, flags=None, delay_step=-1,
+             logits_out=None, stream=None) -> None:
+        rc = lib().zonos2cu_ctx_step(self.h, _ptr(hidden), dtype, C.byref(params), delay_step,
+                                     _ptr(codes), _ptr(flags), _ptr(logits_out), _stream(stream))
+        _check(rc, "zonos2cu_ctx_step")
+
+    def step_host(self, hidden, dtype: int, params: SampleParams, codes, flags=None,
+                  delay_step=-1) -> None:
+        rc = lib().zonos2cu_ctx_step_host(self.h, _ptr(hidden), dtype, C.byref(params),
+                                          delay_step, _ptr(codes), _ptr(flags))
+        _check(rc, "zonos2cu_ctx_step_host")
