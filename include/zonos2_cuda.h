@@ -100,7 +100,8 @@ int zonos2cu_sample_token(uint64_t rng_state[4], const float *logits, int vocab_
 /* One decode step over n_streams x n_cb rows.  Row (s, c) is
  * logits_dev[(s*n_cb + c) * row_stride .. + vocab) (row_stride >= vocab; the
  * reference's [n_tok, 9, 1026] layout is row_stride = 1026).
- *   rng_dev      [n_streams][4] u64: stream s draws one uniform per codebook,
+ *   rng_dev      [n_streams][4] u64, 16-byte aligned: stream s draws one
+ *                uniform per codebook,
  *                in codebook order (the reference's order at
  *                src/zonos2_generate.cpp:259-267), and is advanced by n_cb.
  *   hist_dev     [n_streams][n_cb][hist_len] i32 ring (may be NULL when
@@ -164,8 +165,12 @@ int zonos2cu_get_rng(zonos2cu_ctx *ctx, uint64_t *state_host);
 /* Allow bitmask [n_streams][ceil(vocab/32)]; NULL clears it. */
 int zonos2cu_set_allow(zonos2cu_ctx *ctx, const uint32_t *bits_host);
 
-/* One sampling step from device logits [n_streams][n_cb][row_stride]; the
- * history position advances by one (mod hist_len) on success. */
+/* One sampling step from device logits [n_streams][n_cb][row_stride] on
+ * `stream` (NULL = the legacy default stream, like every "_dev" call); the
+ * history position advances by one (mod hist_len) on success.  The host-path
+ * calls below run on the context's own stream (zonos2cu_ctx_stream): work a
+ * caller enqueues on other streams is not ordered with them, so synchronise
+ * between the two kinds of call. */
 int zonos2cu_ctx_sample(zonos2cu_ctx *ctx, const float *logits_dev, long long row_stride,
                         const zonos2cu_sample_params *params, int delay_step,
                         int32_t *codes_dev, int32_t *flags_dev, void *stream);

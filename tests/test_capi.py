@@ -71,6 +71,7 @@ def test_sample_rows_rejects_bad_arguments(z2):
     assert _rows(z2, H=8, hist=1 << 23, pos=8) == E    # write position outside the ring
     assert _rows(z2, logits=0) == E
     assert _rows(z2, codes=0) == E
+    assert _rows(z2, rng=(1 << 21) + 8) == E           # generator states not 16-byte aligned
     for bad in (dict(temperature=0.0), dict(temperature=float("nan")),
                 dict(temperature=float("inf")), dict(top_p=float("nan")), dict(min_p=1.5),
                 dict(min_p=float("nan")), dict(repetition_penalty=0.0), dict(pad_id=1024),

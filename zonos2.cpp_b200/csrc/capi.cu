@@ -65,6 +65,7 @@ int check_rows(const float *logits, int n_streams, int n_cb, int vocab, long lon
     if (hist_len < 0) return ZONOS2CU_EINVAL;
     if (hist_len > 0 && (!hist || hist_pos < 0 || hist_pos >= hist_len)) return ZONOS2CU_EINVAL;
     if (n_streams > 0 && (!logits || !rng || !codes)) return ZONOS2CU_EINVAL;
+    if ((uintptr_t)rng % 16 != 0) return ZONOS2CU_EINVAL;  // generator states load as 16-byte pairs
     return ZONOS2CU_OK;
 }
 
@@ -459,8 +460,7 @@ int zonos2cu_ctx_sample(zonos2cu_ctx *c, const float *logits_dev, long long row_
     if ((rc = check_params(params, d.vocab))) return rc;
     rc = launch_rows(logits_dev, d.n_streams, d.n_cb, d.vocab, row_stride, params, c->rng,
                      c->hist, d.hist_len, c->hist_pos, c->allow_on ? c->allow : nullptr,
-                     delay_step, codes_dev, flags_dev,
-                     stream ? (cudaStream_t)stream : c->stream);
+                     delay_step, codes_dev, flags_dev, (cudaStream_t)stream);
     if (rc) return rc;
     if (d.hist_len > 0) c->hist_pos = (c->hist_pos + 1) % d.hist_len;
     return ZONOS2CU_OK;
@@ -504,7 +504,7 @@ int zonos2cu_ctx_step(zonos2cu_ctx *c, const void *hidden_dev, zonos2cu_dtype dt
     const zonos2cu_dims &d = c->dims;
     int rc = check_params(params, d.vocab);
     if (rc) return rc;
-    cudaStream_t st = stream ? (cudaStream_t)stream : c->stream;
+    cudaStream_t st = (cudaStream_t)stream;
     float *lg = logits_out_dev ? logits_out_dev : c->logits;
     rc = zonos2cu_head_softcap(c->head, dtype, d.vocab, d.n_cb, d.vocab, d.dim, hidden_dev,
                                d.n_streams, 15.0f, lg, st);

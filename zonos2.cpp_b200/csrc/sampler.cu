@@ -6,26 +6,32 @@
 // forcing, non-finite guard), with the row's uniform drawn from a per-stream
 // Xoshiro256** in codebook order (src/zonos2_generate.cpp:259-267).
 //
-// Layout: one CTA per stream, one warp per codebook row; a row of <= 1024
-// logits lives in 32 registers per lane (lane l, slot (j, e) holds token
+// Layout: one CTA per stream, one warp per codebook row.  A row of <= 1024
+// logits lives in 32 registers per lane (lane l, slot 4*j + e holds token
 // 4*(l + 32*j) + e, so every warp load is a coalesced 128-bit access).
+//
+// Every warp handles its own row: prologue, running max, a 256-bucket
+// histogram of the gap (max - l) in buckets T/8 wide (the last one open), the bucket B* holding
+// the k-th largest logit.  Buckets <= B*+1 are the candidates: a superset of
+// the top-k that also holds every logit whose probability could round equal
+// to the k-th one's (equal probabilities need logits far closer than a
+// bucket).  Candidates are scattered into shared memory in bucket order, get
+// an exact probability, and are put in (p desc, token asc) order by ranking
+// each one inside its bucket; a final adjacency check falls back to a bitonic
+// sort if a probability tie straddles a bucket edge.
+// Then one lane runs the reference's sequential top-k / top-p / min-p sums and
+// CDF walk in its exact order, over quotients p / sum that the whole warp
+// divides out beforehand.  Warp 0 draws the stream's uniforms first and hands
+// each codebook's warp its own through a per-warp named barrier.
 //
 // Exactness: every f32 operation that decides the token is the reference's
 // own operation in the reference's order -- (l - max) / T, exp rounded
-// correctly to f32, the top-k / top-p / min-p sums accumulated sequentially in
-// sorted order by one lane, p / sum divisions, the CDF walk -- so for equal
-// inputs the token equals the reference's up to (a) equal-probability ties,
-// which are taken in ascending token order, and (b) the reference's expf
-// being misrounded by one ulp (glibc, about 1e-4 of inputs).  The file is
-// compiled with -fmad=false so no multiply-add is contracted.
-//
-// Work per row: the full row only passes through cheap per-element steps
-// (prologue, max, a 256-bucket histogram of (max - l) scaled to T/4-wide
-// buckets).  The bucket holding the k-th largest logit plus one bucket of
-// slack bounds the candidate set (a superset of the top-k, including any
-// logit whose probability could round equal to the k-th), and only those
-// candidates get an exact exp, a bitonic sort on (p desc, token asc) keys and
-// the sequential sums.
+// correctly to f32, sums accumulated one term at a time in sorted order,
+// p / sum divisions, the CDF walk -- so for equal inputs the token equals the
+// reference's up to (a) equal-probability ties, taken in ascending token
+// order, and (b) the reference's expf being misrounded by one ulp (glibc, on
+// about 1e-4 of its inputs).  Compiled with -fmad=false: no multiply-add is
+// contracted.
 #include <math.h>
 
 #include "common.cuh"
@@ -35,12 +41,22 @@ namespace z2 {
 
 namespace {
 
-constexpr int kHeader = 128;           // per-CTA uniforms, one per codebook
-constexpr int kRegion = 8192;          // per-warp union region (1024 x u64)
-constexpr int kWarpStride = kRegion + 128;  // + 1024-bit positive map
-constexpr int kHistOffset = 1024;      // bucket histogram after the seen bytes
-constexpr int kQOffset = 2048;         // q = p / sum, when <= 256 keys are sorted
-constexpr int kQCap = 256;
+constexpr int kRegion = 8192;              // per-warp union region (1024 x u64)
+constexpr int kWarpStride = kRegion + 144; // + positive map; 16-byte skew between warps
+constexpr int kPosmapOffset = kRegion;     // 1024-bit map for the zero-probability tail
+constexpr int kBuckets = 128;              // gap buckets: 0..126 finite, 127 masked
+constexpr int kHistOffset = 7680;          // 128 bucket counters at the region's end
+constexpr int kBktOffset = 6656;           // the bucket byte of every slot (1024 bytes)
+constexpr int kScatterMax = 832;           // candidates that fit below the bucket bytes
+constexpr int kRankMax = 256;              // candidates ranked inside their buckets
+// while ranking (<= 256 candidates):
+constexpr int kKeyOffset = 2048;           //   unsorted keys                 [2048, 4096)
+constexpr int kPsOffset = 4096;            //   sorted probabilities          [4096, 5120)
+constexpr int kBucketOffset = 5120;        //   candidate buckets             [5120, 5376)
+// while deciding (<= 256 candidates, keys sorted in [0, 2048)):
+constexpr int kQOffset = 2048;             //   p / sum                       [2048, 3072)
+constexpr int kPfOffset = 3072;            //   prefix sums of the sorted p   [3072, 4096)
+constexpr int kHeader = 64;                // one uniform per codebook
 
 __device__ __forceinline__ float cr_exp(float x)
 {
@@ -55,12 +71,9 @@ __device__ __forceinline__ uint64_t make_key(float p, int tok)
 }
 __device__ __forceinline__ float key_p(uint64_t k) { return __uint_as_float((uint32_t)(k >> 32)); }
 __device__ __forceinline__ int key_tok(uint64_t k) { return (int)(0xffffffffu - (uint32_t)k); }
-
-__device__ __forceinline__ int warp_sum(int x)
+__device__ __forceinline__ uint64_t make_ent(float v, int tok)
 {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) x += __shfl_xor_sync(kFull, x, o);
-    return x;
+    return ((uint64_t)__float_as_uint(v) << 32) | (uint32_t)tok;
 }
 
 __device__ __forceinline__ int warp_incl_scan(int x, int lane)
@@ -73,58 +86,8 @@ __device__ __forceinline__ int warp_incl_scan(int x, int lane)
     return x;
 }
 
-// Descending bitonic sort of 32*E keys held E per lane (element lane*E + r).
-template <int E>
-__device__ __forceinline__ void bitonic_regs_desc(uint64_t (&k)[E], int lane)
-{
-#pragma unroll
-    for (int size = 2; size <= 32 * E; size <<= 1) {
-#pragma unroll
-        for (int stride = size >> 1; stride > 0; stride >>= 1) {
-            if (stride >= E) {
-                const int ls = stride / E;
-                const bool desc = ((lane * E) & size) == 0;
-                const bool lower = ((lane * E) & stride) == 0;
-                const bool keep_max = desc == lower;
-#pragma unroll
-                for (int r = 0; r < E; r++) {
-                    const uint64_t o = __shfl_xor_sync(kFull, k[r], ls);
-                    k[r] = keep_max ? (k[r] > o ? k[r] : o) : (k[r] < o ? k[r] : o);
-                }
-            } else {
-#pragma unroll
-                for (int r = 0; r < E; r++) {
-                    if ((r & stride) == 0) {
-                        const bool desc = ((lane * E + r) & size) == 0;
-                        const uint64_t x = k[r], y = k[r + stride];
-                        const bool sw = desc ? (x < y) : (x > y);
-                        k[r] = sw ? y : x;
-                        k[r + stride] = sw ? x : y;
-                    }
-                }
-            }
-        }
-    }
-}
-
-template <int E>
-__device__ __forceinline__ void sort_keys_regs(uint64_t *ent, int n_c, int lane)
-{
-    uint64_t k[E];
-#pragma unroll
-    for (int r = 0; r < E; r++) {
-        const int i = lane * E + r;
-        k[r] = i < n_c ? ent[i] : 0ull;
-    }
-    __syncwarp();
-    bitonic_regs_desc<E>(k, lane);
-#pragma unroll
-    for (int r = 0; r < E; r++) ent[lane * E + r] = k[r];
-    __syncwarp();
-}
-
 // Descending bitonic sort of n (power of two, <= 1024) keys in shared memory.
-__device__ void bitonic_smem_desc(uint64_t *keys, int n, int lane)
+__device__ __noinline__ void bitonic_smem_desc(uint64_t *keys, int n, int lane)
 {
     for (int size = 2; size <= n; size <<= 1)
         for (int stride = size >> 1; stride > 0; stride >>= 1) {
@@ -142,7 +105,7 @@ __device__ void bitonic_smem_desc(uint64_t *keys, int n, int lane)
         }
 }
 
-// Sequential f32 sum of the probabilities of keys[0..m), in order.
+// Sequential f32 sum of the probabilities of keys[0..m), one term at a time.
 __device__ __forceinline__ float seq_sum(const uint64_t *keys, int m)
 {
     float s = 0.0f;
@@ -161,14 +124,127 @@ __device__ __forceinline__ void mark_seen(unsigned char *seen, int t, int vocab)
     if ((unsigned)t < (unsigned)vocab) seen[t] = 1;
 }
 
-__device__ __forceinline__ void finish_row(const SampleArgs &a, size_t row, int tok, int flag)
+// Gap bucket of a finite logit, 0..126 (the last one open-ended); 127 marks a
+// masked slot.  Buckets stay below 128 so four of them compare against a
+// bound in one 32-bit subtraction.
+__device__ __forceinline__ int bucket_of(float v, float M, float sc)
 {
-    a.codes[row] = tok;
-    if (a.flags) a.flags[row] = flag;
-    if (a.hist && a.hist_len > 0) a.hist[row * (size_t)a.hist_len + a.hist_pos] = tok;
+    return (int)fminf((M - v) * sc, (float)(kBuckets - 2));
+}
+
+// Bit e of the result is set iff byte e of pk is <= bc (bytes and bc < 128).
+__device__ __forceinline__ uint32_t bytes_le(uint32_t pk, uint32_t bc4)
+{
+    const uint32_t le = ((bc4 - pk) & 0x80808080u) >> 7;
+    return (le * 0x10204080u) >> 28;
+}
+
+// Running f32 prefix sums pf[i] = ps[0] + ... + ps[i], one term at a time (one lane).
+__device__ __forceinline__ void prefix_sums(const float *ps, float *pf, int m)
+{
+    float P = 0.0f;
+    int i = 0;
+    for (; i + 4 <= m; i += 4) {
+        const float4 p4 = *reinterpret_cast<const float4 *>(ps + i);
+        float4 o;
+        P += p4.x;
+        o.x = P;
+        P += p4.y;
+        o.y = P;
+        P += p4.z;
+        o.z = P;
+        P += p4.w;
+        o.w = P;
+        *reinterpret_cast<float4 *>(pf + i) = o;
+    }
+    for (; i < m; i++) {
+        P += ps[i];
+        pf[i] = P;
+    }
+}
+
+// 1 + the first i < len whose running sum of ps[j] / S (j <= i, accumulated in
+// order in f32) is >= thr; -1 if none.  The warp divides 32 terms at a time
+// into q, lane 0 accumulates them.
+__device__ int walk_cdf(const float *ps, float *q, int len, float S, float thr, int lane)
+{
+    float cum = 0.0f;
+    for (int base = 0; base < len; base += 32) {
+        const int e = min(base + 32, len);
+        if (base + lane < e) q[base + lane] = ps[base + lane] / S;
+        __syncwarp();
+        int hit = -1;
+        if (lane == 0) {
+            int k = base;
+            for (; k + 4 <= e; k += 4) {
+                const float4 qq = *reinterpret_cast<const float4 *>(q + k);
+                const float c0 = cum + qq.x, c1 = c0 + qq.y, c2 = c1 + qq.z, c3 = c2 + qq.w;
+                if (c3 >= thr) {
+                    hit = c0 >= thr ? k + 1 : c1 >= thr ? k + 2 : c2 >= thr ? k + 3 : k + 4;
+                    break;
+                }
+                cum = c3;
+            }
+            if (hit < 0)
+                for (; k < e; k++) {
+                    cum += q[k];
+                    if (cum >= thr) {
+                        hit = k + 1;
+                        break;
+                    }
+                }
+        }
+        hit = __shfl_sync(kFull, hit, 0);
+        if (hit > 0) return hit;
+    }
+    return -1;
+}
+
+// The (want)-th token, in token order, outside the positive set of a row
+// (keys[0..n_pos)); one lane.
+__device__ int zero_tail_token(const uint64_t *keys, int n_pos, uint32_t *posmap, int V,
+                               int want)
+{
+    for (int w = 0; w < 32; w++) posmap[w] = 0u;
+    for (int i = 0; i < n_pos; i++) {
+        const int t = key_tok(keys[i]);
+        posmap[t >> 5] |= 1u << (t & 31);
+    }
+    for (int w = 0; w < 32; w++) {
+        const int lo = 32 * w;
+        if (lo >= V) break;
+        const uint32_t valid = V - lo >= 32 ? ~0u : ((1u << (V - lo)) - 1u);
+        uint32_t z = ~posmap[w] & valid;
+        const int c = __popc(z);
+        if (want < c) {
+            for (; want > 0; want--) z &= z - 1;
+            return lo + __ffs(z) - 1;
+        }
+        want -= c;
+    }
+    return -1;
 }
 
 }  // namespace
+
+// The build-defined prologue of one logit (slot i of this lane): non-finite
+// guard, repetition penalty, allow / delay mask.
+__device__ __forceinline__ float prologue(float x, int i, uint32_t seenm, uint32_t allowm,
+                                          float rho, float inv_rho)
+{
+    const bool fin = x < INFINITY;  // false for NaN and +inf
+    if ((seenm >> i) & 1u) x = x * (x > 0.0f ? inv_rho : rho);
+    return (fin && ((allowm >> i) & 1u)) ? x : -INFINITY;
+}
+
+__device__ __forceinline__ void named_arrive(int id, int n)
+{
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+__device__ __forceinline__ void named_sync(int id, int n)
+{
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
 
 // MAX_THREADS / MIN_BLOCKS: the 9-codebook model uses <288, 3> (three CTAs,
 // 27 warps per SM at <= 72 registers); wider frames use <512, 1>.
@@ -182,10 +258,15 @@ __global__ void __launch_bounds__(MAX_THREADS, MIN_BLOCKS) sample_kernel(const S
     const int V = a.vocab;
     float *uni = reinterpret_cast<float *>(smem);
     unsigned char *region = smem + kHeader + cb * kWarpStride;
-    uint32_t *posmap = reinterpret_cast<uint32_t *>(region + kRegion);
+    uint64_t *ent = reinterpret_cast<uint64_t *>(region);
+    uint32_t *hist = reinterpret_cast<uint32_t *>(region + kHistOffset);
+    uint32_t *bkt = reinterpret_cast<uint32_t *>(region + kBktOffset);
     const size_t row = (size_t)s * (size_t)a.n_cb + (size_t)cb;
+    const float T = a.temperature;
+    const int K = a.top_k;
+    const bool topk_on = K > 0 && K < V;
 
-    // ---- 1. the logits row -> registers (issued first, consumed in step 4)
+    // ---- 1. the logits row -> registers
     float v[32];
     const float *lrow = a.logits + row * (size_t)a.row_stride;
     if (a.vec_logits) {
@@ -209,7 +290,23 @@ __global__ void __launch_bounds__(MAX_THREADS, MIN_BLOCKS) sample_kernel(const S
             }
     }
 
-    // ---- 2. repetition set: seen[t] = 1 for every token of the history window
+    // ---- 2. the stream's uniforms: warp 0 draws one per codebook, in codebook
+    // order, and releases codebook c's warp through named barrier c
+    if (cb == 0) {
+        if (lane == 0) {
+            ulonglong2 *sp = reinterpret_cast<ulonglong2 *>(a.rng + 4 * (size_t)s);
+            const ulonglong2 st01 = sp[0], st23 = sp[1];
+            Xo256 g{st01.x, st01.y, st23.x, st23.y};
+            for (int c = 0; c < a.n_cb; c++) uni[c] = g.randf();
+            sp[0] = make_ulonglong2(g.s0, g.s1);
+            sp[1] = make_ulonglong2(g.s2, g.s3);
+            __threadfence_block();
+        }
+        __syncwarp();
+        for (int c = 1; c < a.n_cb; c++) named_arrive(c, 64);
+    }
+
+    // ---- 3. repetition set: seen[t] = 1 for every token of the history window
     const bool pen = a.hist_len > 0 && a.rho != 1.0f;
     if (pen) {
         uint4 *seen4 = reinterpret_cast<uint4 *>(region);
@@ -238,289 +335,330 @@ __global__ void __launch_bounds__(MAX_THREADS, MIN_BLOCKS) sample_kernel(const S
         } else {
             for (int q = lane; q < H; q += 32) mark_seen(region, __ldcg(hrow + q), V);
         }
-    }
-
-    // ---- 3. the stream's uniforms: one draw per codebook, in codebook order
-    if (threadIdx.x == 0) {
-        uint64_t *st = a.rng + 4 * (size_t)s;
-        Xo256 g{st[0], st[1], st[2], st[3]};
-        for (int c = 0; c < a.n_cb; c++) uni[c] = g.randf();
-        st[0] = g.s0;
-        st[1] = g.s1;
-        st[2] = g.s2;
-        st[3] = g.s3;
-    }
-    __syncthreads();
-
-    // ---- 4. prologue: non-finite guard, penalty, allow bits, delay forcing
-    const bool force = a.delay_step >= 0 && a.delay_step < cb;
-    uint32_t aw = ~0u;
-    if (a.allow && lane < a.allow_words) aw = __ldg(a.allow + (size_t)s * a.allow_words + lane);
-    bool nonfin = false;
-#pragma unroll
-    for (int j = 0; j < 8; j++) {
-        const int t0 = 4 * (lane + 32 * j);
-        const uint32_t sn = pen ? *reinterpret_cast<const uint32_t *>(region + t0) : 0u;
-        const uint32_t w = __shfl_sync(kFull, aw, (lane + 32 * j) >> 3);
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-            const int t = t0 + e;
-            float x = v[4 * j + e];
-            if (!(x < INFINITY)) {
-                nonfin |= t < V;
-                x = -INFINITY;
-            }
-            if ((sn >> (8 * e)) & 0xffu) x = x > 0.0f ? x * a.inv_rho : x * a.rho;
-            if (!((w >> (t & 31)) & 1u)) x = -INFINITY;
-            if (force && t != a.pad_id) x = -INFINITY;
-            v[4 * j + e] = x;
-        }
-    }
-
-    // ---- 5. running max from -1e9 (src/zonos2_generate.cpp:41-42), liveness
-    float mx = v[0];
-#pragma unroll
-    for (int i = 1; i < 32; i++) mx = fmaxf(mx, v[i]);
-#pragma unroll
-    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
-    const bool live = mx >= -1e9f;
-    const int flag = (__any_sync(kFull, nonfin) ? 2 : 0) | (live ? 0 : 1);
-    if (!live) {
-        if (lane == 0) finish_row(a, row, a.pad_id, flag);
-        return;
-    }
-    const float M = mx;
-    const float T = a.temperature;
-    const int K = a.top_k;
-    const bool topk_on = K > 0 && K < V;
-
-    // ---- 6. candidate bound: bucket of the k-th largest logit, plus one
-    int nf = 0;
-#pragma unroll
-    for (int i = 0; i < 32; i++) nf += v[i] > -INFINITY;
-    const int n_fin = warp_sum(nf);
-    const float bw = fmaxf(T * 0.25f, fabsf(M) * 0x1p-18f + T * 0x1p-14f);
-    const float sc = 1.0f / bw;
-    float sel_lim = INFINITY;  // selected iff finite and (M - v) * sc < sel_lim
-    if (topk_on && n_fin > K) {
-        uint32_t *hist = reinterpret_cast<uint32_t *>(region + kHistOffset);
-        reinterpret_cast<uint4 *>(hist)[2 * lane] = make_uint4(0u, 0u, 0u, 0u);
-        reinterpret_cast<uint4 *>(hist)[2 * lane + 1] = make_uint4(0u, 0u, 0u, 0u);
-        __syncwarp();
-#pragma unroll
-        for (int i = 0; i < 32; i++)
-            if (v[i] > -INFINITY) {
-                const int b = (int)fminf((M - v[i]) * sc, 255.0f);
-                atomicAdd(hist + b, 1u);
-            }
-        __syncwarp();
-        const uint4 h0 = reinterpret_cast<const uint4 *>(hist)[2 * lane];
-        const uint4 h1 = reinterpret_cast<const uint4 *>(hist)[2 * lane + 1];
-        const int hb[8] = {(int)h0.x, (int)h0.y, (int)h0.z, (int)h0.w,
-                           (int)h1.x, (int)h1.y, (int)h1.z, (int)h1.w};
-        int tot = 0;
-#pragma unroll
-        for (int i = 0; i < 8; i++) tot += hb[i];
-        const int incl = warp_incl_scan(tot, lane);
-        const int fl = __ffs(__ballot_sync(kFull, incl >= K)) - 1;  // exists: total > K
-        int bstar = 0;
-        if (lane == fl) {
-            int c = incl - tot;
-#pragma unroll
-            for (int i = 0; i < 8; i++) {
-                c += hb[i];
-                if (c >= K) {
-                    bstar = 8 * lane + i;
-                    break;
-                }
-            }
-        }
-        bstar = __shfl_sync(kFull, bstar, fl);
-        const int bc = min(bstar + 1, 255);
-        if (bc < 255) sel_lim = (float)(bc + 1);
         __syncwarp();
     }
 
-    // ---- 7. compaction of candidates as (logit bits, token)
-    uint64_t *ent = reinterpret_cast<uint64_t *>(region);
-    int n_c;
-    if (topk_on) {
-        // lane-major order: the sort key carries the token, order is irrelevant
-        uint32_t selm = 0;
-#pragma unroll
-        for (int i = 0; i < 32; i++) {
-            const bool sl = v[i] > -INFINITY && (sel_lim == INFINITY || (M - v[i]) * sc < sel_lim);
-            selm |= (uint32_t)sl << i;
-        }
-        const int cnt = __popc(selm);
-        const int incl = warp_incl_scan(cnt, lane);
-        n_c = __shfl_sync(kFull, incl, 31);
-        int off = incl - cnt;
-#pragma unroll
-        for (int i = 0; i < 32; i++)
-            if ((selm >> i) & 1u) {
-                const int t = 4 * (lane + 32 * (i >> 2)) + (i & 3);
-                ent[off++] = ((uint64_t)__float_as_uint(v[i]) << 32) | (uint32_t)t;
-            }
-    } else {
-        // token order: the top-k-off sum runs over the row in token order
-        int base = 0;
+    // ---- 4. prologue: penalty, allow bits, delay forcing, non-finite guard
+    uint32_t seenm = 0u, allowm = ~0u;
+    if (pen) {
 #pragma unroll
         for (int j = 0; j < 8; j++) {
-            int cnt = 0;
+            const uint32_t wd = *reinterpret_cast<const uint32_t *>(region + 4 * (lane + 32 * j));
+            seenm |= ((wd * 0x10204080u) >> 28) << (4 * j);   // four 0/1 bytes -> 4 bits
+        }
+    }
+    if (a.allow) {
+        const uint32_t aw = lane < a.allow_words ? __ldg(a.allow + (size_t)s * a.allow_words + lane)
+                                                 : ~0u;
+        allowm = 0u;
 #pragma unroll
-            for (int e = 0; e < 4; e++) cnt += v[4 * j + e] > -INFINITY;
-            const int incl = warp_incl_scan(cnt, lane);
-            int off = base + incl - cnt;
+        for (int j = 0; j < 8; j++) {
+            const uint32_t w = __shfl_sync(kFull, aw, (lane + 32 * j) >> 3);
+            allowm |= ((w >> (4 * (lane & 7))) & 0xfu) << (4 * j);
+        }
+    }
+    if (a.delay_step >= 0 && a.delay_step < cb) {  // delay pattern: only the pad token
+        const int p = a.pad_id;
+        allowm &= lane == ((p >> 2) & 31) ? (1u << (4 * (p >> 7) + (p & 3))) : 0u;
+    }
+    bool nonfin = false;
+    float mx = -INFINITY;
 #pragma unroll
-            for (int e = 0; e < 4; e++)
-                if (v[4 * j + e] > -INFINITY) {
-                    const int t = 4 * (lane + 32 * j) + e;
-                    ent[off++] = ((uint64_t)__float_as_uint(v[4 * j + e]) << 32) | (uint32_t)t;
-                }
-            base += __shfl_sync(kFull, incl, 31);
-        }
-        n_c = base;
+    for (int i = 0; i < 32; i++) {
+        nonfin |= !(v[i] < INFINITY);
+        v[i] = prologue(v[i], i, seenm, allowm, a.rho, a.inv_rho);
+        mx = fmaxf(mx, v[i]);
     }
-    __syncwarp();
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+    const bool live = mx >= -1e9f;  // running max starts at -1e9: :41-42
+    const int flag = (__any_sync(kFull, nonfin) ? 2 : 0) | (live ? 0 : 1);
 
-    // ---- 8. exact probabilities (src/zonos2_generate.cpp:44-49) as sort keys
-    int np = 0;
-    for (int q = lane; q < n_c; q += 32) {
-        const uint64_t en = ent[q];
-        const float x = __uint_as_float((uint32_t)(en >> 32));
-        const int t = (int)(uint32_t)en;
-        const float p = cr_exp(__fdiv_rn(__fsub_rn(x, M), T));
-        np += p > 0.0f;
-        ent[q] = make_key(p, t);
-    }
-    const int n_pos = warp_sum(np);
-    __syncwarp();
-    float S = 0.0f;
-    if (!topk_on && lane == 0) S = seq_sum(ent, n_c);  // token-order sum
-
-    int N = 32;
-    while (N < n_c) N <<= 1;
-    if (N <= 256) {
-        if (N == 32) sort_keys_regs<1>(ent, n_c, lane);
-        else if (N == 64) sort_keys_regs<2>(ent, n_c, lane);
-        else if (N == 128) sort_keys_regs<4>(ent, n_c, lane);
-        else sort_keys_regs<8>(ent, n_c, lane);
-    } else {
-        for (int i = n_c + lane; i < N; i += 32) ent[i] = 0ull;
+    int tok = a.pad_id;
+    if (live) {
+        const float M = mx;
+        // ---- 5. gap histogram and the bucket of the k-th largest logit
+        const float bw = fmaxf(T * 0.125f, fabsf(M) * 0x1p-18f + T * 0x1p-14f);
+        const float sc = 1.0f / bw;
+        reinterpret_cast<uint4 *>(hist)[lane] = make_uint4(0u, 0u, 0u, 0u);
         __syncwarp();
-        bitonic_smem_desc(ent, N, lane);
-    }
-
-    // ---- 9. top-k / top-p / min-p / draw (src/zonos2_generate.cpp:55-92)
-    // The list is ent[0..m) (positive probabilities, sorted) followed by a
-    // tail of zero-probability tokens in token order, n entries in all.
-    const int n_list = topk_on ? K : V;
-    const int m = min(n_pos, n_list);
-    float *q = reinterpret_cast<float *>(region + kQOffset);
-    const bool use_q = N <= kQCap;
-    if (topk_on && lane == 0) S = seq_sum(ent, m);
-    S = __shfl_sync(kFull, S, 0);
-    int n = n_list;
-
-    if (a.top_p < 1.0f) {
-        if (use_q) {
-            for (int i = lane; i < m; i += 32) q[i] = key_p(ent[i]) / S;
-            __syncwarp();
-        }
-        int cut = -1;
-        if (lane == 0) {
-            float cum = 0.0f;
-            for (int i = 0; i < m; i++) {
-                cum += use_q ? q[i] : key_p(ent[i]) / S;
-                if (cum >= a.top_p) {
-                    cut = i + 1;
-                    break;
-                }
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            uint32_t pk = 0u;
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const float x = v[4 * j + e];
+                const bool fin = x > -INFINITY;
+                const int b = bucket_of(x, M, sc);
+                if (fin) atomicAdd(hist + b, 1u);
+                pk |= (uint32_t)(fin ? b : kBuckets - 1) << (8 * e);
             }
-        }
-        cut = __shfl_sync(kFull, cut, 0);
-        if (cut > 0) n = cut;  // never reached inside the zero tail: cum stops growing
-        if (lane == 0) S = seq_sum(ent, min(n, m));
-        S = __shfl_sync(kFull, S, 0);
-        __syncwarp();
-    }
-
-    if (a.min_p > 0.0f && n > 0) {
-        const float thresh = (key_p(ent[0]) / S) * a.min_p;
-        const int mm = min(n, m);
-        int j = mm;
-        for (int base = 0; base < mm; base += 32) {
-            const int i = base + lane;
-            const bool fail = i < mm && !(key_p(ent[i]) / S >= thresh);
-            const uint32_t b = __ballot_sync(kFull, fail);
-            if (b) {
-                j = base + __ffs(b) - 1;
-                break;
-            }
-        }
-        if (j == mm && n > mm) j = (0.0f >= thresh) ? n : mm;
-        n = j;
-        if (lane == 0) S = seq_sum(ent, min(n, m));
-        S = __shfl_sync(kFull, S, 0);
-    }
-
-    const float r = uni[cb];
-    const int m3 = min(n, m);
-    if (use_q) {
-        for (int i = lane; i < m3; i += 32) q[i] = key_p(ent[i]) / S;
-        __syncwarp();
-    }
-    int pos = -1;
-    if (lane == 0) {
-        float cum = 0.0f;
-        for (int i = 0; i < m3; i++) {
-            cum += use_q ? q[i] : key_p(ent[i]) / S;
-            if (r <= cum) {
-                pos = i;
-                break;
-            }
-        }
-    }
-    pos = __shfl_sync(kFull, pos, 0);
-
-    int tok;
-    if (pos >= 0) {
-        tok = key_tok(ent[pos]);
-    } else if (n > m3) {
-        // fell through to the last list entry, a zero-probability token: the
-        // (n-1-m3)-th token, in token order, outside the positive set
-        posmap[lane] = 0u;
-        __syncwarp();
-        for (int i = lane; i < n_pos; i += 32) {
-            const int t = key_tok(ent[i]);
-            atomicOr(posmap + (t >> 5), 1u << (t & 31));
+            bkt[lane + 32 * j] = pk;
         }
         __syncwarp();
-        const int lo = lane * 32;
-        const uint32_t valid = lo >= V ? 0u : (V - lo >= 32 ? ~0u : ((1u << (V - lo)) - 1u));
-        const uint32_t zw = ~posmap[lane] & valid;
-        const int zc = __popc(zw);
-        const int incl = warp_incl_scan(zc, lane);
-        const int want = n - 1 - m3;
-        const int fl = __ffs(__ballot_sync(kFull, incl > want)) - 1;
-        int t = -1;
-        if (lane == fl) {
-            int kth = want - (incl - zc);
-            for (int b = 0; b < 32; b++)
-                if ((zw >> b) & 1u) {
-                    if (kth == 0) {
-                        t = lo + b;
+        const uint4 h4 = reinterpret_cast<const uint4 *>(hist)[lane];
+        const int h[4] = {(int)h4.x, (int)h4.y, (int)h4.z, (int)h4.w};
+        const int tot = h[0] + h[1] + h[2] + h[3];
+        const int incl = warp_incl_scan(tot, lane);
+        const int n_fin = __shfl_sync(kFull, incl, 31);
+        int bc = kBuckets - 2;   // every finite logit
+        if (topk_on && n_fin > K) {
+            const int fl = __ffs(__ballot_sync(kFull, incl >= K)) - 1;
+            int bstar = 0;
+            if (lane == fl) {
+                int c = incl - tot;
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    c += h[i];
+                    if (c >= K) {
+                        bstar = 4 * lane + i;
                         break;
                     }
-                    kth--;
                 }
+            }
+            bc = min(__shfl_sync(kFull, bstar, fl) + 1, kBuckets - 2);
         }
-        tok = __shfl_sync(kFull, t, fl);
-    } else {
-        tok = n > 0 ? key_tok(ent[n - 1]) : a.pad_id;  // n >= 1 whenever min_p <= 1
+        int n_c;   // candidates: finite logits in buckets 0..bc
+        {
+            int c = incl - tot, upto = 0;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                if (4 * lane + i == bc) upto = c + h[i];
+                c += h[i];
+            }
+            n_c = __shfl_sync(kFull, upto, bc >> 2);
+        }
+        const bool fast = topk_on && n_c <= kScatterMax;
+        const uint32_t bc4 = 0x80808080u | ((uint32_t)bc * 0x01010101u);
+        uint32_t selm = 0u;   // this lane's candidate slots
+#pragma unroll
+        for (int j = 0; j < 8; j++) selm |= bytes_le(bkt[lane + 32 * j], bc4) << (4 * j);
+
+        // ---- 6. candidates -> shared memory as (logit, token).  The row's
+        // registers are gone by now: the few candidates are read again (L1
+        // hits) and pass through the same prologue.
+        if (fast) {
+            {   // exclusive bucket offsets become scatter cursors (bucket order)
+                const int c0 = incl - tot;
+                reinterpret_cast<uint4 *>(hist)[lane] =
+                    make_uint4(c0, c0 + h[0], c0 + h[0] + h[1], c0 + h[0] + h[1] + h[2]);
+                __syncwarp();
+            }
+            uint32_t sm = selm;
+            while (sm) {
+                const int i = __ffs(sm) - 1;
+                sm &= sm - 1;
+                const int t = 4 * (lane + 32 * (i >> 2)) + (i & 3);
+                const float x = prologue(__ldg(lrow + t), i, seenm, allowm, a.rho, a.inv_rho);
+                const int b = (bkt[lane + 32 * (i >> 2)] >> (8 * (i & 3))) & 0xff;
+                const int pos = atomicAdd(hist + b, 1u);
+                ent[pos] = make_ent(x, t);
+            }
+        } else if (topk_on) {
+            // lane-major compaction (the entries may grow over the bucket bytes)
+            const int cnt = __popc(selm);
+            int off = warp_incl_scan(cnt, lane) - cnt;
+            __syncwarp();
+            uint32_t sm = selm;
+            while (sm) {
+                const int i = __ffs(sm) - 1;
+                sm &= sm - 1;
+                const int t = 4 * (lane + 32 * (i >> 2)) + (i & 3);
+                ent[off++] = make_ent(prologue(__ldg(lrow + t), i, seenm, allowm, a.rho, a.inv_rho), t);
+            }
+        } else {
+            // top-k off: every finite logit, in token order (the token-order sum)
+            __syncwarp();
+            int base = 0;
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const uint32_t nib = (selm >> (4 * j)) & 0xfu;
+                const int cnt = __popc(nib);
+                const int inc = warp_incl_scan(cnt, lane);
+                int off = base + inc - cnt;
+#pragma unroll
+                for (int e = 0; e < 4; e++)
+                    if ((nib >> e) & 1u) {
+                        const int t = 4 * (lane + 32 * j) + e;
+                        ent[off++] = make_ent(prologue(__ldg(lrow + t), 4 * j + e, seenm, allowm,
+                                                       a.rho, a.inv_rho), t);
+                    }
+                base += __shfl_sync(kFull, inc, 31);
+            }
+        }
+        __syncwarp();
+
+        // ---- 7. exact probabilities (src/zonos2_generate.cpp:44-49) and order
+        int np = 0;
+        float s0 = 0.0f;
+        const bool small = fast && n_c <= kRankMax;
+        float *ps = reinterpret_cast<float *>(region + kPsOffset);
+        if (small) {
+            // unsorted keys and their buckets beside the (logit, token) entries,
+            // then every key is ranked inside its bucket and stored in place
+            uint64_t *k2 = reinterpret_cast<uint64_t *>(region + kKeyOffset);
+            unsigned char *kb = region + kBucketOffset;
+            for (int q = lane; q < n_c; q += 32) {
+                const uint64_t en = ent[q];
+                const float x = __uint_as_float((uint32_t)(en >> 32));
+                const float p = cr_exp(__fdiv_rn(__fsub_rn(x, M), T));
+                np += p > 0.0f;
+                k2[q] = make_key(p, (int)(uint32_t)en);
+                kb[q] = (unsigned char)bucket_of(x, M, sc);
+            }
+            __syncwarp();
+            for (int q = lane; q < n_c; q += 32) {
+                const uint64_t key = k2[q];
+                const int b = kb[q];
+                const int lo = b ? (int)hist[b - 1] : 0;
+                const int hi = (int)hist[b];
+                int rank = 0;
+                for (int i = lo; i < hi; i++) rank += k2[i] > key;
+                ent[lo + rank] = key;
+                ps[lo + rank] = key_p(key);
+            }
+            __syncwarp();
+            bool bad = false;
+            for (int q = lane; q + 1 < n_c; q += 32) bad |= ent[q] < ent[q + 1];
+            if (__any_sync(kFull, bad)) {   // a probability tie across a bucket edge
+                int N = 32;
+                while (N < n_c) N <<= 1;
+                for (int i = n_c + lane; i < N; i += 32) ent[i] = 0ull;
+                __syncwarp();
+                bitonic_smem_desc(ent, N, lane);
+                for (int q = lane; q < n_c; q += 32) ps[q] = key_p(ent[q]);
+                __syncwarp();
+            }
+        } else {
+            for (int q = lane; q < n_c; q += 32) {
+                const uint64_t en = ent[q];
+                const float x = __uint_as_float((uint32_t)(en >> 32));
+                const float p = cr_exp(__fdiv_rn(__fsub_rn(x, M), T));
+                np += p > 0.0f;
+                ent[q] = make_key(p, (int)(uint32_t)en);
+            }
+            __syncwarp();
+            if (!topk_on && lane == 0) s0 = seq_sum(ent, n_c);  // token-order sum
+            int N = 32;
+            while (N < n_c) N <<= 1;
+            for (int i = n_c + lane; i < N; i += 32) ent[i] = 0ull;
+            __syncwarp();
+            bitonic_smem_desc(ent, N, lane);
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) np += __shfl_xor_sync(kFull, np, o);
+        const int n_pos = np;
+        s0 = __shfl_sync(kFull, s0, 0);
+
+        // ---- 8. top-k / top-p / min-p (src/zonos2_generate.cpp:55-84).  The
+        // list is ent[0..m) (positive probabilities, sorted) followed by
+        // zero-probability tokens in token order, n entries in all.  Every
+        // sum the reference recomputes from zero over a sorted prefix is one
+        // entry of the running prefix sums.
+        const int n_list = topk_on ? K : V;
+        const int m = min(n_pos, n_list);
+        int n = n_list;
+        int pos = -1;
+        if (small) {
+            float *pf = reinterpret_cast<float *>(region + kPfOffset);
+            float *q = reinterpret_cast<float *>(region + kQOffset);
+            if (lane == 0) prefix_sums(ps, pf, m);
+            __syncwarp();
+            float S = topk_on ? pf[m - 1] : s0;
+            if (a.top_p < 1.0f) {
+                const int cut = walk_cdf(ps, q, m, S, a.top_p, lane);
+                if (cut > 0) n = cut;  // never inside the zero tail: the sum stops growing
+                S = pf[min(n, m) - 1];
+            }
+            if (a.min_p > 0.0f && n > 0) {
+                const float thresh = (ps[0] / S) * a.min_p;
+                const int mm = min(n, m);
+                int j = mm;
+                for (int base = 0; base < mm; base += 32) {
+                    const int i = base + lane;
+                    const uint32_t fails = __ballot_sync(kFull, i < mm && !(ps[i] / S >= thresh));
+                    if (fails) {
+                        j = base + __ffs(fails) - 1;
+                        break;
+                    }
+                }
+                if (j == mm && n > mm) j = (0.0f >= thresh) ? n : mm;
+                n = j;
+                S = pf[min(n, m) - 1];
+            }
+            if (cb > 0) named_sync(cb, 64);   // this codebook's uniform is in shared memory
+            // ---- 9. one uniform, CDF walk (src/zonos2_generate.cpp:86-92)
+            const int hit = walk_cdf(ps, q, min(n, m), S, uni[cb], lane);
+            pos = hit > 0 ? hit - 1 : -1;
+        } else {
+            float S = topk_on ? (lane == 0 ? seq_sum(ent, m) : 0.0f) : s0;
+            S = __shfl_sync(kFull, S, 0);
+            if (a.top_p < 1.0f) {
+                int cut = -1;
+                if (lane == 0) {
+                    float cum = 0.0f;
+                    for (int i = 0; i < m; i++) {
+                        cum += key_p(ent[i]) / S;
+                        if (cum >= a.top_p) {
+                            cut = i + 1;
+                            break;
+                        }
+                    }
+                    S = seq_sum(ent, min(cut > 0 ? cut : n, m));
+                }
+                cut = __shfl_sync(kFull, cut, 0);
+                S = __shfl_sync(kFull, S, 0);
+                if (cut > 0) n = cut;
+            }
+            if (a.min_p > 0.0f && n > 0) {
+                const float thresh = (key_p(ent[0]) / S) * a.min_p;
+                const int mm = min(n, m);
+                int j = mm;
+                for (int base = 0; base < mm; base += 32) {
+                    const int i = base + lane;
+                    const uint32_t fails =
+                        __ballot_sync(kFull, i < mm && !(key_p(ent[i]) / S >= thresh));
+                    if (fails) {
+                        j = base + __ffs(fails) - 1;
+                        break;
+                    }
+                }
+                if (j == mm && n > mm) j = (0.0f >= thresh) ? n : mm;
+                n = j;
+                if (lane == 0) S = seq_sum(ent, min(n, m));
+                S = __shfl_sync(kFull, S, 0);
+            }
+            if (cb > 0) named_sync(cb, 64);
+            if (lane == 0) {
+                const float u = uni[cb];
+                float cum = 0.0f;
+                for (int i = 0; i < min(n, m); i++) {
+                    cum += key_p(ent[i]) / S;
+                    if (u <= cum) {
+                        pos = i;
+                        break;
+                    }
+                }
+            }
+            pos = __shfl_sync(kFull, pos, 0);
+        }
+        if (lane == 0) {
+            const int m3 = min(n, m);
+            if (pos >= 0) tok = key_tok(ent[pos]);
+            else if (n > m3)   // the last entry is a zero-probability token
+                tok = zero_tail_token(ent, n_pos,
+                                      reinterpret_cast<uint32_t *>(region + kPosmapOffset), V,
+                                      n - 1 - m3);
+            else if (n > 0) tok = key_tok(ent[n - 1]);
+        }
+    } else if (cb > 0) {
+        named_sync(cb, 64);
     }
-    if (lane == 0) finish_row(a, row, tok, flag);
+    if (lane == 0) {
+        a.codes[row] = tok;
+        if (a.flags) a.flags[row] = flag;
+        if (a.hist && a.hist_len > 0) a.hist[row * (size_t)a.hist_len + a.hist_pos] = tok;
+    }
 }
 
 size_t sample_smem_bytes(int n_cb) { return (size_t)kHeader + (size_t)n_cb * kWarpStride; }
