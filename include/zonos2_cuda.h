@@ -143,7 +143,7 @@ typedef struct {
     int n_cb;        /* codebooks per frame: 9                                     */
     int vocab;       /* sampled tokens per codebook: 1024                          */
     int dim;         /* hidden size for the fused head: 2048 (0: sampler only)     */
-    int hist_len;    /* repetition-history window per row (0: none)                */
+    int hist_len;    /* repetition-history window per row (0: none; <= 65535)      */
     uint64_t seed;   /* stream s uses Xoshiro256(seed + first_stream + s)          */
     uint64_t first_stream; /* global index of this shard's first stream           */
 } zonos2cu_dims;
@@ -156,7 +156,11 @@ int zonos2cu_ctx_destroy(zonos2cu_ctx *ctx);
  * rows of each codebook are kept on the device). */
 int zonos2cu_set_head(zonos2cu_ctx *ctx, const void *W_host, zonos2cu_dtype dtype,
                       int rows_per_cb);
-/* History ring [n_streams][n_cb][hist_len] and its write position. */
+/* History ring [n_streams][n_cb][hist_len] and its write position.  The
+ * context also keeps, per row, how often each token occurs in the ring and a
+ * bitmap of the tokens present, updated by every step for the token it evicts
+ * and the one it appends: the penalty reads 128 bytes per row instead of the
+ * whole ring. */
 int zonos2cu_set_history(zonos2cu_ctx *ctx, const int32_t *hist_host, int hist_pos);
 int zonos2cu_get_history(zonos2cu_ctx *ctx, int32_t *hist_host, int *hist_pos);
 /* Generator states [n_streams][4]. */

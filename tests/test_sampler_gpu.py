@@ -275,3 +275,40 @@ def test_context_rollout_and_host_path(z2, oracle, cuda):
     assert pos == 6 and (h == hist).all()
     assert (ctx.get_rng() == rng).all()
     ctx.close()
+
+
+@pytest.mark.parametrize("H", [1, 6, 37, 1024])
+def test_context_incremental_history_rollout(z2, oracle, cuda, H):
+    """The context keeps token counts + a presence bitmap instead of scanning the
+    ring; over a long rollout with heavy eviction and repeats the codes must
+    equal the oracle's full-ring scan every step (low temperature: repeats)."""
+    import torch
+    S, Cb, V = 12, 9, 1024
+    rs = np.random.default_rng(H)
+    ctx = z2.Context(0, S, Cb, V, 0, H, seed=31)
+    hist = rs.integers(-2, 40, (S, Cb, H), dtype=np.int32)   # few distinct tokens, empties
+    ctx.set_history(hist, H - 1)
+    prm = make_params(0.3, 20, 0.95, 0.0, 1.7, 1023)
+    p = z2.SampleParams(0.3, 20, 0.95, 0.0, 1.7, 1023)
+    rng = oracle.rng_seed_streams(31, S)
+    pos = H - 1
+    codes = torch.zeros((S, Cb), dtype=torch.int32, device=cuda)
+    for step in range(40):
+        lg = softcapped(rs, (S, Cb, V), 1.0)
+        lg[:, :, :48] += 3.0                     # keep sampling the same few tokens
+        oc, _, _ = oracle.step(lg, prm, rng, hist, hist_pos=pos, exp_mode=1)
+        ctx.sample(_t(lg, cuda), p, codes)
+        torch.cuda.synchronize()
+        assert (codes.cpu().numpy() == oc).all(), step
+        pos = (pos + 1) % H
+    h, hp = ctx.get_history()
+    assert hp == pos and (h == hist).all()
+    # re-indexing from a new ring mid-rollout
+    hist2 = rs.integers(0, V, (S, Cb, H), dtype=np.int32)
+    ctx.set_history(hist2, 0)
+    lg = softcapped(rs, (S, Cb, V), 2.0)
+    oc, _, _ = oracle.step(lg, prm, rng, hist2, hist_pos=0, exp_mode=1)
+    ctx.sample(_t(lg, cuda), p, codes)
+    torch.cuda.synchronize()
+    assert (codes.cpu().numpy() == oc).all()
+    ctx.close()

@@ -52,6 +52,7 @@ void fill_sample_args(z2::SampleArgs &a, const zonos2cu_sample_params *p)
     a.min_p = p->min_p;
     a.rho = p->repetition_penalty;
     a.inv_rho = 1.0f / p->repetition_penalty;
+    a.inv_temp = 1.0 / (double)p->temperature;
     a.pad_id = p->pad_id;
 }
 
@@ -72,7 +73,8 @@ int check_rows(const float *logits, int n_streams, int n_cb, int vocab, long lon
 int launch_rows(const float *logits, int n_streams, int n_cb, int vocab, long long row_stride,
                 const zonos2cu_sample_params *params, uint64_t *rng, int32_t *hist,
                 int hist_len, int hist_pos, const uint32_t *allow, int delay_step,
-                int32_t *codes, int32_t *flags, cudaStream_t stream)
+                int32_t *codes, int32_t *flags, cudaStream_t stream,
+                uint16_t *counts = nullptr, uint32_t *presence = nullptr)
 {
     z2::SampleArgs a{};
     a.logits = logits;
@@ -92,6 +94,8 @@ int launch_rows(const float *logits, int n_streams, int n_cb, int vocab, long lo
     a.flags = flags;
     a.vec_logits = (row_stride % 4 == 0) && (vocab % 4 == 0) && ((uintptr_t)logits % 16 == 0);
     a.vec_hist = hist_len > 0 && (hist_len % 4 == 0) && ((uintptr_t)hist % 16 == 0);
+    a.counts = hist_len > 0 ? counts : nullptr;
+    a.presence = hist_len > 0 ? presence : nullptr;
     Z2_CK(z2::launch_sample(a, stream));
     return ZONOS2CU_OK;
 }
@@ -247,6 +251,8 @@ struct zonos2cu_ctx {
     uint64_t *rng = nullptr;     // [S][4]
     int32_t *hist = nullptr;     // [S][C][H]
     int hist_pos = 0;
+    uint16_t *counts = nullptr;  // [S][C][V] occurrences of each token in the ring
+    uint32_t *presence = nullptr;// [S][C][words] tokens with a nonzero count
     uint32_t *allow = nullptr;   // [S][words]
     bool allow_on = false;
     void *head = nullptr;        // [C*V][D] of head_dtype
@@ -307,6 +313,7 @@ int zonos2cu_ctx_create(int device, const zonos2cu_dims *d, zonos2cu_ctx **out)
         d->dim < 0 || d->hist_len < 0)
         return ZONOS2CU_EINVAL;
     if (d->vocab > z2::kSamplerVocabMax) return ZONOS2CU_EUNSUPPORTED;
+    if (d->hist_len > 65535) return ZONOS2CU_EUNSUPPORTED;  // 16-bit token counts
     int ndev = 0;
     Z2_CK(cudaGetDeviceCount(&ndev));
     if (device < 0 || device >= ndev) return ZONOS2CU_EINVAL;
@@ -330,9 +337,16 @@ int zonos2cu_ctx_create(int device, const zonos2cu_dims *d, zonos2cu_ctx **out)
         delete[] h;
         if (e != cudaSuccess) { rc = cuda_fail(e, "rng upload"); break; }
         if (d->hist_len > 0) {
-            const size_t hb = sizeof(int32_t) * S * d->n_cb * (size_t)d->hist_len;
+            const size_t rows = S * d->n_cb;
+            const size_t hb = sizeof(int32_t) * rows * (size_t)d->hist_len;
+            const size_t cbytes = sizeof(uint16_t) * rows * (size_t)d->vocab;
+            const size_t pbytes = sizeof(uint32_t) * rows * (size_t)((d->vocab + 31) / 32);
             e = cudaMalloc(&c->hist, hb);
             if (e == cudaSuccess) e = cudaMemset(c->hist, 0xff, hb);  // -1: empty slots
+            if (e == cudaSuccess) e = cudaMalloc(&c->counts, cbytes);
+            if (e == cudaSuccess) e = cudaMemset(c->counts, 0, cbytes);
+            if (e == cudaSuccess) e = cudaMalloc(&c->presence, pbytes);
+            if (e == cudaSuccess) e = cudaMemset(c->presence, 0, pbytes);
             if (e != cudaSuccess) { rc = cuda_fail(e, "history"); break; }
         }
     } while (0);
@@ -351,6 +365,8 @@ int zonos2cu_ctx_destroy(zonos2cu_ctx *c)
     if (c->stream) cudaStreamSynchronize(c->stream);
     cudaFree(c->rng);
     cudaFree(c->hist);
+    cudaFree(c->counts);
+    cudaFree(c->presence);
     cudaFree(c->allow);
     cudaFree(c->head);
     cudaFree(c->logits);
@@ -391,9 +407,13 @@ int zonos2cu_set_history(zonos2cu_ctx *c, const int32_t *hist_host, int hist_pos
     if (!c || !hist_host || c->dims.hist_len < 1) return ZONOS2CU_EINVAL;
     if (hist_pos < 0 || hist_pos >= c->dims.hist_len) return ZONOS2CU_EINVAL;
     DeviceGuard g(c->device);
-    if (n_rows(c))
+    if (n_rows(c)) {
         Z2_CK(cudaMemcpy(c->hist, hist_host, sizeof(int32_t) * n_rows(c) * c->dims.hist_len,
                          cudaMemcpyHostToDevice));
+        Z2_CK(z2::launch_history_index(c->hist, (long long)n_rows(c), c->dims.hist_len,
+                                       c->dims.vocab, c->counts, c->presence, c->stream));
+        Z2_CK(cudaStreamSynchronize(c->stream));
+    }
     c->hist_pos = hist_pos;
     return ZONOS2CU_OK;
 }
@@ -460,7 +480,8 @@ int zonos2cu_ctx_sample(zonos2cu_ctx *c, const float *logits_dev, long long row_
     if ((rc = check_params(params, d.vocab))) return rc;
     rc = launch_rows(logits_dev, d.n_streams, d.n_cb, d.vocab, row_stride, params, c->rng,
                      c->hist, d.hist_len, c->hist_pos, c->allow_on ? c->allow : nullptr,
-                     delay_step, codes_dev, flags_dev, (cudaStream_t)stream);
+                     delay_step, codes_dev, flags_dev, (cudaStream_t)stream, c->counts,
+                     c->presence);
     if (rc) return rc;
     if (d.hist_len > 0) c->hist_pos = (c->hist_pos + 1) % d.hist_len;
     return ZONOS2CU_OK;
