@@ -1,0 +1,87 @@
+"""Output head + softcap on the GPU against the oracle, through the C ABI.
+
+f32 weights: the GEMV accumulates in f64, so its logits sit within the
+reference's own sequential-f32 rounding of the oracle's: |d| <= 1e-5 * max(1, |ref|).
+bf16 weights and hidden states: the tcgen05 GEMM multiplies the same bf16
+values exactly and accumulates in f32; the stated bf16 tolerance is 2e-2, and
+the test also bounds the error observed (f32 summation order only) by 1e-3.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+F32_TOL = 1e-5
+BF16_TOL = 2e-2
+
+
+def _bf16(x):
+    import workloads as W
+    return W.to_bf16_bits(x), W.from_bf16_bits(W.to_bf16_bits(x))
+
+
+def _dev(x, cuda):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(x)).to(cuda)
+
+
+@pytest.mark.parametrize("B,rpc", [(1, 1026), (2, 1024), (5, 1026)])
+def test_head_f32_gemv(z2, oracle, cuda, B, rpc):
+    import torch
+    rs = np.random.default_rng(42 + B)
+    W = rs.normal(0, 0.02, size=(9 * rpc, 2048)).astype(np.float32)
+    h = rs.normal(0, 1, size=(B, 2048)).astype(np.float32)
+    h[-1] *= 30.0                                  # saturate the softcap on one row
+    out = torch.empty((B, 9, 1024), dtype=torch.float32, device=cuda)
+    z2.head_softcap(_dev(W, cuda), z2.F32, rpc, 9, 1024, _dev(h, cuda), out)
+    torch.cuda.synchronize()
+    ref = oracle.head_softcap(W, rpc, 9, 1024, h)
+    got = out.cpu().numpy()
+    # config-1 rows (hidden ~ N(0,1)): within 1e-5 relative
+    err = np.abs(got[:-1] - ref[:-1]) / np.maximum(1.0, np.abs(ref[:-1]))
+    assert err.size == 0 or err.max() <= F32_TOL, err.max()
+    # the saturating row: the oracle's own sequential f32 sum is only within
+    # n * 2^-24 * sum|h_i w_i| of the exact dot product, which the GPU computes
+    Wr = W.reshape(9, rpc, 2048)[:, :1024]
+    bound = 2048 * 2.0**-24 * (np.abs(Wr) @ np.abs(h[-1]))
+    assert (np.abs(got[-1] - ref[-1]) <= F32_TOL * np.maximum(1.0, np.abs(ref[-1])) + bound).all()
+
+
+@pytest.mark.parametrize("B,rpc", [(1, 1026), (3, 1024), (128, 1026), (200, 1024), (256, 1026),
+                                   (300, 1026)])
+def test_head_bf16_tcgen05(z2, oracle, cuda, B, rpc):
+    import torch
+    rs = np.random.default_rng(7 + B)
+    Wb, Wf = _bf16(rs.normal(0, 0.02, size=(9 * rpc, 2048)).astype(np.float32))
+    hb, hf = _bf16(rs.normal(0, 1, size=(B, 2048)).astype(np.float32))
+    out = torch.full((B, 9, 1024), float("nan"), dtype=torch.float32, device=cuda)
+    z2.head_softcap(_dev(Wb, cuda), z2.BF16, rpc, 9, 1024, _dev(hb, cuda), out)
+    torch.cuda.synchronize()
+    assert z2.device_error() == 0
+    ref = oracle.head_softcap(Wf, rpc, 9, 1024, hf)
+    got = out.cpu().numpy()
+    assert np.isfinite(got).all()
+    err = np.abs(got - ref)
+    print(f"B={B}: max |d| {err.max():.2e}")
+    assert err.max() <= BF16_TOL
+    assert err.max() <= 1e-3
+
+
+def test_head_bf16_large_batch_rows(z2, oracle, cuda):
+    """A 4096-row launch (persistent tiles, both accumulators): rows spot-checked."""
+    import torch
+    rs = np.random.default_rng(11)
+    B = 4096
+    Wb, Wf = _bf16(rs.normal(0, 0.02, size=(9 * 1024, 2048)).astype(np.float32))
+    hb, hf = _bf16(rs.normal(0, 1, size=(B, 2048)).astype(np.float32))
+    out = torch.empty((B, 9, 1024), dtype=torch.float32, device=cuda)
+    z2.head_softcap(_dev(Wb, cuda), z2.BF16, 1024, 9, 1024, _dev(hb, cuda), out)
+    torch.cuda.synchronize()
+    assert z2.device_error() == 0
+    rows = np.array([0, 1, 127, 128, 2047, 2048, 3333, 4095])
+    ref = oracle.head_softcap(Wf, 1024, 9, 1024, hf[rows])
+    got = out.cpu().numpy()[rows]
+    assert np.abs(got - ref).max() <= 1e-3
+    # every row against a torch f32 matmul of the same bf16 values
+    full = torch.tanh(torch.from_numpy(hf).to(cuda) @ torch.from_numpy(Wf).to(cuda).T / 15) * 15
+    assert (out.reshape(B, -1) - full).abs().max().item() <= 1e-3

@@ -1,4 +1,30 @@
 // head_tc.cu -- bf16 output head + softcap on the tcgen05 tensor cores (sm_100a).
+//
+// Restates the multi_output head of the reference -- linear_forward
+// (src/zonos2_model.cpp:200-216, :687-690) followed by l = 15*tanh(l/15)
+// (:692-703) -- for the sampled rows of each codebook, as one GEMM
+//     logits[b, c*V + v] = softcap(sum_k hidden[b, k] * W[c*rpc + v, k])
+// with bf16 operands and f32 accumulation.
+//
+// Persistent kernel, one CTA per SM, three warp roles:
+//   warp 0      TMA producer: 128 x 64 tiles of hidden (A) and BN x 64 tiles of
+//               W (B), 128-byte swizzled, into a ring of shared-memory stages;
+//   warp 1      allocates TMEM and issues tcgen05.mma (M=128, N=BN, K=16) from
+//               one elected lane, accumulating a 128 x BN f32 tile in TMEM;
+//               two accumulators alternate so the epilogue of one tile
+//               overlaps the MMAs of the next;
+//   warps 2..5  epilogue: tcgen05.ld of their 32 TMEM lanes, softcap, f32 store.
+// Stages hand over through mbarriers: TMA completes `full`, tcgen05.commit
+// releases `empty` and signals `tfull`, the epilogue releases `tempty`.
+// Every wait is bounded: after ~2 s it records an error in g_device_error and
+// the kernel winds down (in-flight copies waited for, TMEM freed).
+// No TMA load here uses cluster multicast.
+#include <cuda.h>
+#include <math.h>
+#include <stdio.h>
+
+#include <mutex>
+
 #include "common.cuh"
 #include "head.cuh"
 
@@ -18,6 +44,397 @@ int read_and_clear_device_error(int *value)
     return 0;
 }
 
-cudaError_t launch_head_tc_bf16(const HeadArgs &, cudaStream_t) { return cudaErrorNotSupported; }
+namespace {
+
+constexpr int kBM = 128;            // rows of hidden per tile (TMEM lanes)
+constexpr int kBK = 64;             // bf16 elements per 128-byte swizzled row
+constexpr int kThreads = 192;       // 6 warps
+constexpr unsigned long long kWaitNs = 2000000000ull;
+
+enum : int { kErrTimeout = 1 };
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p)
+{
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Waits for the phase with this parity to complete; false after ~2 s (the
+// error word is set, the caller winds down).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity)
+{
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 1;; it++) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 255u) == 0u && globaltimer_ns() - t0 > kWaitNs) {
+            atomicCAS(&g_device_error, 0, kErrTimeout);
+            return false;
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y,
+                                            uint32_t bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void prefetch_map(const CUtensorMap *map)
+{
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// Shared-memory matrix descriptor, K-major, 128-byte swizzle: 8-row groups of
+// 128-byte rows, 1024 bytes apart (SBO); version 1 (sm_100); base offset 0
+// (stages are 1024-byte aligned).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr)
+{
+    return (uint64_t)((addr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) |
+           ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t idesc, uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32])
+{
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+          "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+          "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+struct TcArgs {
+    int batch, n_cb, vocab, rows_per_cb, dim;
+    int tiles_m, tiles_n, n_tiles;
+    float softcap;
+    float *out;  // [batch][n_cb * vocab]
+};
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    head_tc_kernel(const __grid_constant__ CUtensorMap map_a,
+                   const __grid_constant__ CUtensorMap map_b, const TcArgs args)
+{
+    constexpr uint32_t kABytes = kBM * kBK * 2;
+    constexpr uint32_t kBBytes = BN * kBK * 2;
+    constexpr uint32_t kStageBytes = kABytes + kBBytes;
+    constexpr uint32_t kTmemCols = 2 * BN;
+    // tcgen05 kind::f16 instruction descriptor: D f32, A and B bf16, both
+    // K-major, N = BN, M = 128.
+    constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                ((uint32_t)(kBM >> 4) << 24);
+
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *smem = reinterpret_cast<unsigned char *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * kStageBytes);
+    // bars: full[STAGES], empty[STAGES], tfull[2], tempty[2]; then the TMEM slot
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 4);
+    __shared__ int s_abort;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int KB = args.dim / kBK;
+    auto full = [&](int s) { return smem_u32(bars + s); };
+    auto empty = [&](int s) { return smem_u32(bars + STAGES + s); };
+    auto tfull = [&](int a) { return smem_u32(bars + 2 * STAGES + a); };
+    auto tempty = [&](int a) { return smem_u32(bars + 2 * STAGES + 2 + a); };
+
+    if (threadIdx.x == 0) {
+        s_abort = 0;
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(full(s), 1);
+            mbar_init(empty(s), 1);
+        }
+        for (int a = 0; a < 2; a++) {
+            mbar_init(tfull(a), 1);
+            mbar_init(tempty(a), 128);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        prefetch_map(&map_a);
+        prefetch_map(&map_b);
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ---- TMA producer
+        if (lane == 0) {
+            int it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < args.n_tiles && ok; tile += gridDim.x) {
+                const int mt = tile % args.tiles_m, nt = tile / args.tiles_m;
+                const int per_cb = args.vocab / BN;
+                const int c = nt / per_cb, t = nt % per_cb;
+                const int a_row = mt * kBM;
+                const int b_row = c * args.rows_per_cb + t * BN;
+                for (int kb = 0; kb < KB; kb++, it++) {
+                    const int s = it % STAGES;
+                    const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+                    if (!mbar_wait(empty(s), ph ^ 1u) || *(volatile int *)&s_abort) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t sa = smem_u32(smem + s * kStageBytes);
+                    mbar_expect_tx(full(s), kStageBytes);
+                    tma_load_2d(sa, &map_a, kb * kBK, a_row, full(s));
+                    tma_load_2d(sa + kABytes, &map_b, kb * kBK, b_row, full(s));
+                }
+            }
+            if (!ok) {
+                s_abort = 1;
+                // copies still in flight land before the CTA leaves
+                for (int k = 0; k < STAGES && k < it; k++) {
+                    const int j = it - 1 - k;
+                    mbar_wait(full(j % STAGES), (uint32_t)(j / STAGES) & 1u);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---- MMA issuer
+        if (lane == 0) {
+            int it = 0, local = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < args.n_tiles && ok; tile += gridDim.x, local++) {
+                const int acc = local & 1;
+                const uint32_t aph = (uint32_t)(local >> 1) & 1u;
+                if (!mbar_wait(tempty(acc), aph ^ 1u)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+                for (int kb = 0; kb < KB; kb++, it++) {
+                    const int s = it % STAGES;
+                    const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+                    if (!mbar_wait(full(s), ph) || *(volatile int *)&s_abort) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(smem + s * kStageBytes);
+                    const uint64_t ad = sw128_desc(sa), bd = sw128_desc(sa + kABytes);
+#pragma unroll
+                    for (int k = 0; k < kBK / 16; k++)   // 32 bytes of K per instruction
+                        mma_bf16(d_tmem, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), kIdesc,
+                                 (kb | k) != 0);
+                    mma_commit(empty(s));
+                }
+                if (ok) mma_commit(tfull(acc));
+            }
+            if (!ok) s_abort = 1;
+        }
+    } else {
+        // ---- epilogue: TMEM -> softcap -> global
+        const int q = warp & 3;   // the TMEM lane quarter this warp may read
+        int local = 0;
+        for (int tile = blockIdx.x; tile < args.n_tiles; tile += gridDim.x, local++) {
+            const int acc = local & 1;
+            const uint32_t aph = (uint32_t)(local >> 1) & 1u;
+            if (!mbar_wait(tfull(acc), aph)) {
+                s_abort = 1;
+                break;
+            }
+            if (*(volatile int *)&s_abort) break;
+            tc_fence_after();
+            const int mt = tile % args.tiles_m, nt = tile / args.tiles_m;
+            const int row = mt * kBM + 32 * q + lane;
+            float *orow = args.out + (size_t)row * (size_t)(args.n_cb * args.vocab) +
+                          (size_t)nt * BN;
+            const float cap = args.softcap;
+#pragma unroll 1
+            for (int ch = 0; ch < BN / 32; ch++) {
+                uint32_t r[32];
+                tmem_ld32(tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BN + 32 * ch), r);
+                if (row < args.batch) {
+                    float4 *dst = reinterpret_cast<float4 *>(orow + 32 * ch);
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        float o[4];
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            const float l = __uint_as_float(r[4 * i + e]);
+                            o[e] = cap > 0.0f ? cap * tanhf(l / cap) : l;
+                        }
+                        dst[i] = make_float4(o[0], o[1], o[2], o[3]);
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(tempty(acc));
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                     "r"(kTmemCols)
+                     : "memory");
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn()
+{
+    static std::once_flag once;
+    static EncodeTiledFn fn = nullptr;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// 2-D bf16 tensor map over rows x cols (cols contiguous), box box_cols x box_rows.
+bool make_map(CUtensorMap *m, const void *base, uint64_t rows, uint64_t cols, uint32_t box_rows)
+{
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kBK, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides,
+               box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+           CUDA_SUCCESS;
+}
+
+template <int BN, int STAGES>
+cudaError_t launch_bn(const HeadArgs &a, const CUtensorMap &ma, int tiles_m, int sms,
+                      cudaStream_t stream)
+{
+    static bool attr[64] = {false};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const size_t smem = (size_t)STAGES * (kBM + BN) * kBK * 2 + 1024 + 256;
+    if (dev < 64 && !attr[dev]) {
+        e = cudaFuncSetAttribute(head_tc_kernel<BN, STAGES>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        attr[dev] = true;
+    }
+    CUtensorMap mb;
+    if (!make_map(&mb, a.W, (uint64_t)a.n_cb * a.rows_per_cb, (uint64_t)a.dim, BN))
+        return cudaErrorInvalidValue;
+    TcArgs t;
+    t.batch = a.batch;
+    t.n_cb = a.n_cb;
+    t.vocab = a.vocab;
+    t.rows_per_cb = a.rows_per_cb;
+    t.dim = a.dim;
+    t.tiles_m = tiles_m;
+    t.tiles_n = a.n_cb * (a.vocab / BN);
+    t.n_tiles = t.tiles_m * t.tiles_n;
+    t.softcap = a.softcap;
+    t.out = a.out;
+    const int grid = t.n_tiles < sms ? t.n_tiles : sms;
+    head_tc_kernel<BN, STAGES><<<grid, kThreads, smem, stream>>>(ma, mb, t);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_head_tc_bf16(const HeadArgs &a, cudaStream_t stream)
+{
+    if (a.batch == 0) return cudaSuccess;
+    if (a.dim % kBK != 0 || a.vocab % 64 != 0 || a.rows_per_cb < a.vocab)
+        return cudaErrorNotSupported;
+    if ((uintptr_t)a.W % 16 != 0 || (uintptr_t)a.hidden % 16 != 0 || (uintptr_t)a.out % 16 != 0)
+        return cudaErrorNotSupported;
+    int dev = 0, sms = 148;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    CUtensorMap ma;
+    if (!make_map(&ma, a.hidden, (uint64_t)a.batch, (uint64_t)a.dim, kBM))
+        return cudaErrorInvalidValue;
+    const int tiles_m = (a.batch + kBM - 1) / kBM;
+    // the widest N tile that still gives every SM work
+    const int cols = a.n_cb * a.vocab;
+    if (a.vocab % 256 == 0 && tiles_m * (cols / 256) >= sms)
+        return launch_bn<256, 4>(a, ma, tiles_m, sms, stream);
+    if (a.vocab % 128 == 0 && tiles_m * (cols / 128) >= sms)
+        return launch_bn<128, 6>(a, ma, tiles_m, sms, stream);
+    return launch_bn<64, 8>(a, ma, tiles_m, sms, stream);
+}
 
 }  // namespace z2
