@@ -50,10 +50,14 @@ WORKLOAD = ("constrained sampling, 4096 streams x 9 codebooks x 1024 vocab per G
             "logits ~N(0,4^2), 1% +8 spikes, softcap 15; delay masks over a 128-step rollout; "
             "70% allow bitmask; top-k 100, top-p 0.9, min-p 0.02, T 0.7; penalty 1.1 over "
             "1024-entry history")
-# Algorithmic bytes of one (stream, codebook) row: logits read + history read
-# + history append + code write + allow bits (per stream, /9) + generator
-# state read and write (per stream, /9).
-ROW_BYTES = 4 * VOCAB + 4 * HIST + 4 + 4 + 128 / NCB + 64 / NCB
+# Algorithmic bytes of one (stream, codebook) row, the scope table's figure:
+# logits read + history read + token write and history append + allow bits
+# (one 128-byte mask per stream, shared by its 9 rows).
+ROW_BYTES = 4 * VOCAB + 4 * HIST + 8 + 128 / NCB
+# What the decode context actually has to move per row: logits, the 128-byte
+# presence bitmap of the history instead of the ring, ring read + write,
+# two u16 counts read and written, code and flag, allow bits, generator state.
+DESIGN_ROW_BYTES = 4 * VOCAB + 128 + 8 + 8 + 8 + 128 / NCB + 64 / NCB
 
 
 def dist_env():
@@ -342,7 +346,9 @@ def run_ours(args):
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": args.traffic,
                      "kernel": "sample_kernel<288,3>", "kernel_ms": kern_ms,
-                     "bytes_per_launch": launch_bytes, "peak_source": peak_src},
+                     "bytes_per_launch": launch_bytes, "peak_source": peak_src,
+                     "design_bytes_per_launch": DESIGN_ROW_BYTES * rows,
+                     "design_frac": DESIGN_ROW_BYTES * rows / (kern_ms / 1e3) / 1e9 / peak},
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": "codes/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps},
