@@ -151,6 +151,9 @@ typedef struct {
 int zonos2cu_ctx_create(int device, const zonos2cu_dims *dims, zonos2cu_ctx **out);
 int zonos2cu_ctx_destroy(zonos2cu_ctx *ctx);
 
+/* The setters and getters below synchronise the device: they are set-up calls,
+ * safe against steps enqueued on any stream, not per-step calls. */
+
 /* Head weights from host memory, [n_cb*rows_per_cb][dim] of dtype
  * (rows_per_cb = 1026 for the reference's output.bin; only the first vocab
  * rows of each codebook are kept on the device). */
@@ -198,6 +201,7 @@ void *zonos2cu_ctx_stream(zonos2cu_ctx *ctx);
 /* Reads and clears the device-side error word that bounded waits set when
  * they expire (synchronises the current device).  0 = no error. */
 int zonos2cu_device_error(void);
+
 
 #ifdef __cplusplus
 }

@@ -333,7 +333,8 @@ int zonos2cu_ctx_create(int device, const zonos2cu_dims *d, zonos2cu_ctx **out)
         uint64_t *h = new (std::nothrow) uint64_t[4 * S];
         if (!h) { rc = ZONOS2CU_ENOMEM; break; }
         for (size_t s = 0; s < S; s++) zonos2cu_rng_seed(d->seed + d->first_stream + s, h + 4 * s);
-        e = cudaMemcpy(c->rng, h, sizeof(uint64_t) * 4 * S, cudaMemcpyHostToDevice);
+        e = cudaMemcpyAsync(c->rng, h, sizeof(uint64_t) * 4 * S, cudaMemcpyHostToDevice, c->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
         delete[] h;
         if (e != cudaSuccess) { rc = cuda_fail(e, "rng upload"); break; }
         if (d->hist_len > 0) {
@@ -342,11 +343,12 @@ int zonos2cu_ctx_create(int device, const zonos2cu_dims *d, zonos2cu_ctx **out)
             const size_t cbytes = sizeof(uint16_t) * rows * (size_t)d->vocab;
             const size_t pbytes = sizeof(uint32_t) * rows * (size_t)((d->vocab + 31) / 32);
             e = cudaMalloc(&c->hist, hb);
-            if (e == cudaSuccess) e = cudaMemset(c->hist, 0xff, hb);  // -1: empty slots
+            if (e == cudaSuccess) e = cudaMemsetAsync(c->hist, 0xff, hb, c->stream);  // -1: empty
             if (e == cudaSuccess) e = cudaMalloc(&c->counts, cbytes);
-            if (e == cudaSuccess) e = cudaMemset(c->counts, 0, cbytes);
+            if (e == cudaSuccess) e = cudaMemsetAsync(c->counts, 0, cbytes, c->stream);
             if (e == cudaSuccess) e = cudaMalloc(&c->presence, pbytes);
-            if (e == cudaSuccess) e = cudaMemset(c->presence, 0, pbytes);
+            if (e == cudaSuccess) e = cudaMemsetAsync(c->presence, 0, pbytes, c->stream);
+            if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
             if (e != cudaSuccess) { rc = cuda_fail(e, "history"); break; }
         }
     } while (0);
@@ -385,6 +387,7 @@ int zonos2cu_set_head(zonos2cu_ctx *c, const void *W_host, zonos2cu_dtype dtype,
     if (!c || !W_host || c->dims.dim < 1 || rows_per_cb < c->dims.vocab) return ZONOS2CU_EINVAL;
     if (dtype != ZONOS2CU_F32 && dtype != ZONOS2CU_BF16) return ZONOS2CU_EINVAL;
     DeviceGuard g(c->device);
+    Z2_CK(cudaDeviceSynchronize());   // no step may still be using the state
     const size_t es = dtype == ZONOS2CU_F32 ? 4 : 2;
     const size_t row_bytes = es * (size_t)c->dims.dim;
     const size_t V = (size_t)c->dims.vocab, C = (size_t)c->dims.n_cb;
@@ -394,9 +397,10 @@ int zonos2cu_set_head(zonos2cu_ctx *c, const void *W_host, zonos2cu_dtype dtype,
     // keep the sampled rows of each codebook: one 2-D copy per codebook
     for (size_t cb = 0; cb < C; cb++) {
         const char *src = static_cast<const char *>(W_host) + cb * (size_t)rows_per_cb * row_bytes;
-        Z2_CK(cudaMemcpy(static_cast<char *>(c->head) + cb * V * row_bytes, src, V * row_bytes,
-                         cudaMemcpyHostToDevice));
+        Z2_CK(cudaMemcpyAsync(static_cast<char *>(c->head) + cb * V * row_bytes, src, V * row_bytes,
+                              cudaMemcpyHostToDevice, c->stream));
     }
+    Z2_CK(cudaStreamSynchronize(c->stream));
     c->head_dtype = dtype;
     if (!c->logits && n_rows(c)) Z2_CK(cudaMalloc(&c->logits, sizeof(float) * n_rows(c) * V));
     return ZONOS2CU_OK;
@@ -407,9 +411,10 @@ int zonos2cu_set_history(zonos2cu_ctx *c, const int32_t *hist_host, int hist_pos
     if (!c || !hist_host || c->dims.hist_len < 1) return ZONOS2CU_EINVAL;
     if (hist_pos < 0 || hist_pos >= c->dims.hist_len) return ZONOS2CU_EINVAL;
     DeviceGuard g(c->device);
+    Z2_CK(cudaDeviceSynchronize());   // no step may still be using the state
     if (n_rows(c)) {
-        Z2_CK(cudaMemcpy(c->hist, hist_host, sizeof(int32_t) * n_rows(c) * c->dims.hist_len,
-                         cudaMemcpyHostToDevice));
+        Z2_CK(cudaMemcpyAsync(c->hist, hist_host, sizeof(int32_t) * n_rows(c) * c->dims.hist_len,
+                              cudaMemcpyHostToDevice, c->stream));
         Z2_CK(z2::launch_history_index(c->hist, (long long)n_rows(c), c->dims.hist_len,
                                        c->dims.vocab, c->counts, c->presence, c->stream));
         Z2_CK(cudaStreamSynchronize(c->stream));
@@ -422,7 +427,7 @@ int zonos2cu_get_history(zonos2cu_ctx *c, int32_t *hist_host, int *hist_pos)
 {
     if (!c || c->dims.hist_len < 1) return ZONOS2CU_EINVAL;
     DeviceGuard g(c->device);
-    Z2_CK(cudaStreamSynchronize(c->stream));
+    Z2_CK(cudaDeviceSynchronize());   // steps may have run on any stream
     if (hist_host && n_rows(c))
         Z2_CK(cudaMemcpy(hist_host, c->hist, sizeof(int32_t) * n_rows(c) * c->dims.hist_len,
                          cudaMemcpyDeviceToHost));
@@ -434,9 +439,11 @@ int zonos2cu_set_rng(zonos2cu_ctx *c, const uint64_t *state_host)
 {
     if (!c || !state_host) return ZONOS2CU_EINVAL;
     DeviceGuard g(c->device);
+    Z2_CK(cudaDeviceSynchronize());   // no step may still be using the state
     if (c->dims.n_streams)
-        Z2_CK(cudaMemcpy(c->rng, state_host, sizeof(uint64_t) * 4 * c->dims.n_streams,
-                         cudaMemcpyHostToDevice));
+        Z2_CK(cudaMemcpyAsync(c->rng, state_host, sizeof(uint64_t) * 4 * c->dims.n_streams,
+                              cudaMemcpyHostToDevice, c->stream));
+    Z2_CK(cudaStreamSynchronize(c->stream));
     return ZONOS2CU_OK;
 }
 
@@ -444,7 +451,7 @@ int zonos2cu_get_rng(zonos2cu_ctx *c, uint64_t *state_host)
 {
     if (!c || !state_host) return ZONOS2CU_EINVAL;
     DeviceGuard g(c->device);
-    Z2_CK(cudaStreamSynchronize(c->stream));
+    Z2_CK(cudaDeviceSynchronize());   // steps may have run on any stream
     if (c->dims.n_streams)
         Z2_CK(cudaMemcpy(state_host, c->rng, sizeof(uint64_t) * 4 * c->dims.n_streams,
                          cudaMemcpyDeviceToHost));
@@ -455,6 +462,7 @@ int zonos2cu_set_allow(zonos2cu_ctx *c, const uint32_t *bits_host)
 {
     if (!c) return ZONOS2CU_EINVAL;
     DeviceGuard g(c->device);
+    Z2_CK(cudaDeviceSynchronize());   // no step may still be using the state
     if (!bits_host) {
         c->allow_on = false;
         return ZONOS2CU_OK;
@@ -462,7 +470,9 @@ int zonos2cu_set_allow(zonos2cu_ctx *c, const uint32_t *bits_host)
     const size_t words = (size_t)(c->dims.vocab + 31) / 32 * c->dims.n_streams;
     if (!c->allow && words) Z2_CK(cudaMalloc(&c->allow, sizeof(uint32_t) * words));
     if (words)
-        Z2_CK(cudaMemcpy(c->allow, bits_host, sizeof(uint32_t) * words, cudaMemcpyHostToDevice));
+        Z2_CK(cudaMemcpyAsync(c->allow, bits_host, sizeof(uint32_t) * words, cudaMemcpyHostToDevice,
+                              c->stream));
+    Z2_CK(cudaStreamSynchronize(c->stream));
     c->allow_on = true;
     return ZONOS2CU_OK;
 }
