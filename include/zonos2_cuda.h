@@ -45,6 +45,7 @@ extern "C" {
 #define ZONOS2CU_ESTATE (-4)       /* context not ready (e.g. no head weights set) */
 #define ZONOS2CU_EUNSUPPORTED (-5) /* shape outside what the kernels implement     */
 #define ZONOS2CU_EDEVICE (-6)      /* a kernel reported a bounded wait that expired */
+#define ZONOS2CU_ETOOBIG (-7)      /* larger than zonos2cu_step_noalloc's fixed scratch */
 
 /* ---- per-row flags written next to each sampled code ---------------------- */
 #define ZONOS2CU_FLAG_ALL_MASKED 1 /* no logit >= -1e9 survived: code = pad_id     */
@@ -202,6 +203,32 @@ void *zonos2cu_ctx_stream(zonos2cu_ctx *ctx);
  * they expire (synchronises the current device).  0 = no error. */
 int zonos2cu_device_error(void);
 
+/* ---- one decode step that allocates nothing -------------------------------- */
+
+/* No counterpart in the reference.  For callers that may not allocate device
+ * memory -- a host application whose device memory belongs to another
+ * framework's pool, or a real-time decode loop where an allocation could
+ * block or synchronise the device.  It runs zonos2cu_head_softcap and then
+ * zonos2cu_sample_rows (same arguments, same results) with the intermediate
+ * logits in a fixed device array compiled into the library: every GPU that
+ * loads the library holds ZONOS2CU_NOALLOC_MAX_LOGITS floats (2.25 MiB) of it
+ * until the process exits, and no call allocates or frees anything.
+ *   - n_streams * n_cb * vocab must not exceed ZONOS2CU_NOALLOC_MAX_LOGITS
+ *     (64 streams of 9 x 1024): larger requests return ZONOS2CU_ETOOBIG.
+ *   - The first call on a device looks the array's device address up
+ *     (cudaGetSymbolAddress, with that device current); make that first call
+ *     before any stream capture.
+ *   - All calls on a device share the one array: calls whose work overlaps on
+ *     the GPU race.  Order them on one stream, or synchronise between them.
+ * Arguments are those of the two entry points it combines (softcap 15 in
+ * the model; row stride of the logits = vocab). */
+#define ZONOS2CU_NOALLOC_MAX_LOGITS (64 * 9 * 1024)
+int zonos2cu_step_noalloc(const void *W_dev, zonos2cu_dtype dtype, int rows_per_cb, int n_cb,
+                          int vocab, int dim, const void *hidden_dev, int n_streams, float softcap,
+                          const zonos2cu_sample_params *params, uint64_t *rng_dev,
+                          int32_t *hist_dev, int hist_len, int hist_pos,
+                          const uint32_t *allow_dev, int delay_step, int32_t *codes_dev,
+                          int32_t *flags_dev, void *stream);
 
 #ifdef __cplusplus
 }

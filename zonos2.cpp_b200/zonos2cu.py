@@ -25,7 +25,8 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libzonos2cu.so")
 
-OK, EINVAL, ECUDA, ENOMEM, ESTATE, EUNSUPPORTED, EDEVICE = 0, -1, -2, -3, -4, -5, -6
+OK, EINVAL, ECUDA, ENOMEM, ESTATE, EUNSUPPORTED, EDEVICE, ETOOBIG = 0, -1, -2, -3, -4, -5, -6, -7
+NOALLOC_MAX_LOGITS = 64 * 9 * 1024
 FLAG_ALL_MASKED, FLAG_NONFINITE = 1, 2
 F32, BF16 = 0, 1
 
@@ -36,13 +37,14 @@ EXPORTS = (
     "zonos2cu_get_history", "zonos2cu_set_rng", "zonos2cu_get_rng", "zonos2cu_set_allow",
     "zonos2cu_ctx_sample", "zonos2cu_ctx_sample_host", "zonos2cu_ctx_step",
     "zonos2cu_ctx_step_host", "zonos2cu_ctx_stream", "zonos2cu_device_error",
+    "zonos2cu_step_noalloc",
 )
 
 
 class Zonos2cuError(RuntimeError):
     def __init__(self, code: int, what: str):
         names = {EINVAL: "EINVAL", ECUDA: "ECUDA", ENOMEM: "ENOMEM", ESTATE: "ESTATE",
-                 EUNSUPPORTED: "EUNSUPPORTED", EDEVICE: "EDEVICE"}
+                 EUNSUPPORTED: "EUNSUPPORTED", EDEVICE: "EDEVICE", ETOOBIG: "ETOOBIG"}
         msg = f"{what} failed: {names.get(code, code)}"
         detail = last_error() if _lib is not None else ""
         if detail:
@@ -102,6 +104,8 @@ def lib() -> C.CDLL:
         "zonos2cu_ctx_step_host": (i, [vp, vp, i, C.POINTER(SampleParams), i, vp, vp]),
         "zonos2cu_ctx_stream": (vp, [vp]),
         "zonos2cu_device_error": (i, []),
+        "zonos2cu_step_noalloc": (i, [vp, i, i, i, i, i, vp, i, f, C.POINTER(SampleParams), vp,
+                                      vp, i, i, vp, i, vp, vp, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -191,6 +195,20 @@ def head_softcap(W, dtype: int, rows_per_cb: int, n_cb: int, vocab: int, hidden,
     rc = lib().zonos2cu_head_softcap(_ptr(W), dtype, rows_per_cb, n_cb, vocab, D, _ptr(hidden), B,
                                      softcap, _ptr(out), _stream(stream))
     _check(rc, "zonos2cu_head_softcap")
+
+
+def step_noalloc(W, dtype: int, rows_per_cb: int, n_cb: int, vocab: int, hidden, params,
+                 rng, codes, *, flags=None, hist=None, hist_pos=0, allow=None, delay_step=-1,
+                 softcap: float = 15.0, stream=None) -> None:
+    """Head + softcap + sampler with the logits in the library's fixed array
+    (no device allocation; at most NOALLOC_MAX_LOGITS logits per call)."""
+    S, D = hidden.shape
+    H = 0 if hist is None else hist.shape[-1]
+    rc = lib().zonos2cu_step_noalloc(_ptr(W), dtype, rows_per_cb, n_cb, vocab, D, _ptr(hidden), S,
+                                     softcap, C.byref(params), _ptr(rng), _ptr(hist), H, hist_pos,
+                                     _ptr(allow), delay_step, _ptr(codes), _ptr(flags),
+                                     _stream(stream))
+    _check(rc, "zonos2cu_step_noalloc")
 
 
 def device_error() -> int:
