@@ -192,6 +192,60 @@ def make_device_inputs(torch, dev, rank: int, n_batches: int = 2):
     return batches, hist, allow
 
 
+def measure_head(torch, Z, dev, stream, reps: int = 20):
+    """The tcgen05 head GEMM (bf16, f32 accumulate, softcap epilogue) at the
+    fused configurations' batch sizes, and the fused decode step at 4096
+    streams (head + sampler, penalty 1.2 over 1024, top-k 50, top-p 0.95)."""
+    import workloads as W
+    out = {}
+    g = torch.Generator(device=dev)
+    g.manual_seed(2024)
+    Wt = (torch.randn((NCB * VOCAB, 2048), generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    peaks = {}
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except Exception:
+        pass
+    tpeak = float(peaks.get("bf16_tflops", 1590.0))
+    for B in (256, 4096):
+        h = torch.randn((B, 2048), generator=g, device=dev).to(torch.bfloat16)
+        lg = torch.empty((B, NCB, VOCAB), dtype=torch.float32, device=dev)
+        for _ in range(3):
+            Z.head_softcap(Wt, Z.BF16, VOCAB, NCB, VOCAB, h, lg, stream=stream)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            Z.head_softcap(Wt, Z.BF16, VOCAB, NCB, VOCAB, h, lg, stream=stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        flops = 2.0 * B * 2048 * NCB * VOCAB
+        out[f"gemm_b{B}"] = {"ms": ms, "tflops": flops / (ms / 1e3) / 1e12,
+                             "frac_of_bf16_peak": flops / (ms / 1e3) / 1e12 / tpeak}
+    # the fused decode step, 4096 streams
+    S = 4096
+    cfg = W.CONFIGS[5]
+    ctx = Z.Context(dev.index, S, NCB, VOCAB, 2048, HIST, seed=cfg.seed)
+    ctx.set_head(W.to_bf16_bits(W.head_weights(cfg, rows_per_cb=VOCAB)), Z.BF16, VOCAB)
+    ctx.set_history(W.initial_history(cfg, S), 0)
+    p = Z.SampleParams(cfg.temperature, cfg.top_k, cfg.top_p, cfg.min_p, cfg.penalty, PAD)
+    h = torch.randn((S, 2048), generator=g, device=dev).to(torch.bfloat16)
+    codes = torch.zeros((S, NCB), dtype=torch.int32, device=dev)
+    for _ in range(3):
+        ctx.step(h, Z.BF16, p, codes, stream=stream)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        ctx.step(h, Z.BF16, p, codes, stream=stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    out["fused_step_b4096"] = {"ms": ms, "codes_per_s": S * NCB / (ms / 1e3)}
+    ctx.close()
+    return out
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -307,6 +361,7 @@ def run_ours(args):
     d2h = int(rows * 4 * (2 if ws == 1 else ws)) if rank == 0 else 0
 
     ctx.close()
+    head = measure_head(torch, Z, dev, stream) if (rank == 0 and not args.no_head) else None
     if rank != 0:
         if ws > 1:
             dist.barrier()
@@ -353,6 +408,7 @@ def run_ours(args):
         "e2e": {"value": e2e_value, "unit": "codes/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps},
         "gpu_launches": args.steps,
+        "head": head,
         "clocks": clocks.result() if clocks else None,
     }
     print(json.dumps(line), flush=True)
@@ -369,6 +425,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-streams", type=int, default=1024)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-head", action="store_true", help="skip the head GEMM / fused timing")
     ap.add_argument("--traffic", type=float, default=None,
                     help="ncu dram bytes per sampler launch, when measured")
     args = ap.parse_args()
