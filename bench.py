@@ -58,6 +58,10 @@ ROW_BYTES = 4 * VOCAB + 4 * HIST + 8 + 128 / NCB
 # presence bitmap of the history instead of the ring, ring read + write,
 # two u16 counts read and written, code and flag, allow bits, generator state.
 DESIGN_ROW_BYTES = 4 * VOCAB + 128 + 8 + 8 + 8 + 128 / NCB + 64 / NCB
+# DRAM bytes (read + write) of one sample_kernel<288,3> launch on this
+# workload, from an ncu capture of `bench.py --steps 3 --warmup 3`
+# (dram__bytes_read.sum 170.35 MB + dram__bytes_write.sum 9.60 MB).
+SAMPLER_TRAFFIC_BYTES = 179.94e6
 
 
 def dist_env():
@@ -192,6 +196,35 @@ def make_device_inputs(torch, dev, rank: int, n_batches: int = 2):
     return batches, hist, allow
 
 
+def _bf16_peak():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f).get("bf16_tflops", 1590.0))
+    except Exception:
+        return 1590.0
+
+
+def time_head_gemm(torch, Z, dev, stream, Wt, B, g, reps: int = 20, warm: int = 3):
+    """CUDA-event time of the bf16 head GEMM + softcap at batch B (ms/launch)."""
+    h = torch.randn((B, 2048), generator=g, device=dev).to(torch.bfloat16)
+    lg = torch.empty((B, NCB, VOCAB), dtype=torch.float32, device=dev)
+    for _ in range(warm):
+        Z.head_softcap(Wt, Z.BF16, VOCAB, NCB, VOCAB, h, lg, stream=stream)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        Z.head_softcap(Wt, Z.BF16, VOCAB, NCB, VOCAB, h, lg, stream=stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / max(reps, 1)
+    tflops = 2.0 * B * 2048 * NCB * VOCAB / (ms / 1e3) / 1e12
+    return {"ms": ms, "tflops": tflops, "frac_of_bf16_peak": tflops / _bf16_peak()}
+
+
+def head_weights_dev(torch, dev, g):
+    return (torch.randn((NCB * VOCAB, 2048), generator=g, device=dev) * 0.02).to(torch.bfloat16)
+
+
 def measure_head(torch, Z, dev, stream, reps: int = 20):
     """The tcgen05 head GEMM (bf16, f32 accumulate, softcap epilogue) at the
     fused configurations' batch sizes, and the fused decode step at 4096
@@ -200,29 +233,9 @@ def measure_head(torch, Z, dev, stream, reps: int = 20):
     out = {}
     g = torch.Generator(device=dev)
     g.manual_seed(2024)
-    Wt = (torch.randn((NCB * VOCAB, 2048), generator=g, device=dev) * 0.02).to(torch.bfloat16)
-    peaks = {}
-    try:
-        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
-            peaks = json.load(f)
-    except Exception:
-        pass
-    tpeak = float(peaks.get("bf16_tflops", 1590.0))
+    Wt = head_weights_dev(torch, dev, g)
     for B in (256, 4096):
-        h = torch.randn((B, 2048), generator=g, device=dev).to(torch.bfloat16)
-        lg = torch.empty((B, NCB, VOCAB), dtype=torch.float32, device=dev)
-        for _ in range(3):
-            Z.head_softcap(Wt, Z.BF16, VOCAB, NCB, VOCAB, h, lg, stream=stream)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(reps):
-            Z.head_softcap(Wt, Z.BF16, VOCAB, NCB, VOCAB, h, lg, stream=stream)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1) / reps
-        flops = 2.0 * B * 2048 * NCB * VOCAB
-        out[f"gemm_b{B}"] = {"ms": ms, "tflops": flops / (ms / 1e3) / 1e12,
-                             "frac_of_bf16_peak": flops / (ms / 1e3) / 1e12 / tpeak}
+        out[f"gemm_b{B}"] = time_head_gemm(torch, Z, dev, stream, Wt, B, g, reps)
     # the fused decode step, 4096 streams
     S = 4096
     cfg = W.CONFIGS[5]
@@ -246,12 +259,32 @@ def measure_head(torch, Z, dev, stream, reps: int = 20):
     return out
 
 
+def run_head_only(args):
+    """Only the head GEMM at batch --head-only (warm-up, then --steps launches):
+    the small case the head kernel is profiled on."""
+    import torch
+    import zonos2cu as Z
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(2024)
+    Wt = head_weights_dev(torch, dev, g)
+    r = time_head_gemm(torch, Z, dev, torch.cuda.current_stream(), Wt, args.head_only, g,
+                       reps=args.steps, warm=args.warmup)
+    err = Z.device_error()
+    print(json.dumps({"head_only": args.head_only, **r, "device_error": err}), flush=True)
+    if err:
+        sys.exit(1)
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
+    import sharding
     import zonos2cu as Z
 
     ws, rank, local = dist_env()
+    first, _ = sharding.shard_range(ws * STREAMS, ws, rank)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if ws > 1:
@@ -265,20 +298,23 @@ def run_ours(args):
         torch.cuda.synchronize()
 
     batches, hist, allow = make_device_inputs(torch, dev, rank)
-    ctx = Z.Context(local, STREAMS, NCB, VOCAB, 0, HIST, seed=1234, first_stream=rank * STREAMS)
+    ctx = Z.Context(local, STREAMS, NCB, VOCAB, 0, HIST, seed=1234, first_stream=first)
     ctx.set_history(hist, 0)
     ctx.set_allow(allow)
     params = Z.SampleParams(TEMP, TOPK, TOPP, MINP, RHO, PAD)
     codes = torch.zeros((STREAMS, NCB), dtype=torch.int32, device=dev)
     flags = torch.zeros((STREAMS, NCB), dtype=torch.int32, device=dev)
-    gathered = torch.zeros((ws, STREAMS, NCB), dtype=torch.int32, device=dev)
+    gathered = torch.zeros((ws * STREAMS, NCB), dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream()
+
+    def gather():
+        sharding.gather_codes(codes, ws * STREAMS, ws, rank, out=gathered)
 
     def step(t):
         ctx.sample(batches[t % len(batches)], params, codes, flags, delay_step=t % ROLLOUT,
                    stream=stream)
         if ws > 1:
-            dist.all_gather_into_tensor(gathered, codes)
+            gather()
 
     clocks = ClockSampler(local) if rank == 0 else None
 
@@ -301,7 +337,7 @@ def run_ours(args):
                    stream=stream)
         k_end[i].record(stream)
         if ws > 1:
-            dist.all_gather_into_tensor(gathered, codes)
+            gather()
     t_end.record(stream)
     barrier()
     if clocks:
@@ -329,9 +365,9 @@ def run_ours(args):
         else:
             dev_in.copy_(hb, non_blocking=True)
             ctx.sample(dev_in, params, codes, flags, delay_step=t % ROLLOUT, stream=stream)
-            dist.all_gather_into_tensor(gathered, codes)
+            gather()
             if rank == 0:
-                host_codes.copy_(gathered, non_blocking=True)
+                host_codes.view(ws * STREAMS, NCB).copy_(gathered, non_blocking=True)
             stream.synchronize()
 
     e2e_steps = max(1, min(args.steps, 64))
@@ -426,12 +462,16 @@ def main():
     ap.add_argument("--cpu-streams", type=int, default=1024)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-head", action="store_true", help="skip the head GEMM / fused timing")
-    ap.add_argument("--traffic", type=float, default=None,
+    ap.add_argument("--head-only", type=int, default=0, metavar="B",
+                    help="time only the bf16 head GEMM at batch B (profiling case)")
+    ap.add_argument("--traffic", type=float, default=SAMPLER_TRAFFIC_BYTES,
                     help="ncu dram bytes per sampler launch, when measured")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         run_reference(args)
+    elif args.head_only:
+        run_head_only(args)
     else:
         run_ours(args)
 
