@@ -74,7 +74,8 @@ int launch_rows(const float *logits, int n_streams, int n_cb, int vocab, long lo
                 const zonos2cu_sample_params *params, uint64_t *rng, int32_t *hist,
                 int hist_len, int hist_pos, const uint32_t *allow, int delay_step,
                 int32_t *codes, int32_t *flags, cudaStream_t stream,
-                uint16_t *counts = nullptr, uint32_t *presence = nullptr)
+                uint16_t *counts = nullptr, uint32_t *presence = nullptr,
+                bool allow_lane_major = false)
 {
     z2::SampleArgs a{};
     a.logits = logits;
@@ -89,6 +90,7 @@ int launch_rows(const float *logits, int n_streams, int n_cb, int vocab, long lo
     a.hist_pos = hist_pos;
     a.allow = allow;
     a.allow_words = (vocab + 31) / 32;
+    a.allow_lane_major = allow_lane_major ? 1 : 0;
     a.delay_step = delay_step;
     a.codes = codes;
     a.flags = flags;
@@ -234,10 +236,11 @@ int zonos2cu_head_softcap(const void *W_dev, zonos2cu_dtype dtype, int rows_per_
 int zonos2cu_device_error(void)
 {
     Z2_CK(cudaDeviceSynchronize());
-    int v = 0;
-    const int e = z2::read_and_clear_device_error(&v);
+    int v = 0, vs = 0;
+    int e = z2::read_and_clear_device_error(&v);
+    if (!e) e = z2::read_and_clear_sampler_error(&vs);
     if (e) return cuda_fail((cudaError_t)e, "device error word");
-    return v;
+    return v ? v : vs;
 }
 
 }  // extern "C"
@@ -252,8 +255,8 @@ struct zonos2cu_ctx {
     int32_t *hist = nullptr;     // [S][C][H]
     int hist_pos = 0;
     uint16_t *counts = nullptr;  // [S][C][V] occurrences of each token in the ring
-    uint32_t *presence = nullptr;// [S][C][words] tokens with a nonzero count
-    uint32_t *allow = nullptr;   // [S][words]
+    uint32_t *presence = nullptr;// [S][C][32] tokens with a nonzero count, lane-major
+    uint32_t *allow = nullptr;   // [S][32] lane-major (word l, bit 4j+e: token 4(l+32j)+e)
     bool allow_on = false;
     void *head = nullptr;        // [C*V][D] of head_dtype
     zonos2cu_dtype head_dtype = ZONOS2CU_F32;
@@ -341,7 +344,7 @@ int zonos2cu_ctx_create(int device, const zonos2cu_dims *d, zonos2cu_ctx **out)
             const size_t rows = S * d->n_cb;
             const size_t hb = sizeof(int32_t) * rows * (size_t)d->hist_len;
             const size_t cbytes = sizeof(uint16_t) * rows * (size_t)d->vocab;
-            const size_t pbytes = sizeof(uint32_t) * rows * (size_t)((d->vocab + 31) / 32);
+            const size_t pbytes = sizeof(uint32_t) * rows * 32;   // lane-major 1024-bit map
             e = cudaMalloc(&c->hist, hb);
             if (e == cudaSuccess) e = cudaMemsetAsync(c->hist, 0xff, hb, c->stream);  // -1: empty
             if (e == cudaSuccess) e = cudaMalloc(&c->counts, cbytes);
@@ -467,12 +470,25 @@ int zonos2cu_set_allow(zonos2cu_ctx *c, const uint32_t *bits_host)
         c->allow_on = false;
         return ZONOS2CU_OK;
     }
-    const size_t words = (size_t)(c->dims.vocab + 31) / 32 * c->dims.n_streams;
-    if (!c->allow && words) Z2_CK(cudaMalloc(&c->allow, sizeof(uint32_t) * words));
-    if (words)
-        Z2_CK(cudaMemcpyAsync(c->allow, bits_host, sizeof(uint32_t) * words, cudaMemcpyHostToDevice,
-                              c->stream));
-    Z2_CK(cudaStreamSynchronize(c->stream));
+    // stored lane-major: the sampler's lane l reads word l of its stream
+    const size_t S = (size_t)c->dims.n_streams;
+    const int V = c->dims.vocab, words = (V + 31) / 32;
+    if (S) {
+        uint32_t *lm = new (std::nothrow) uint32_t[32 * S]();
+        if (!lm) return ZONOS2CU_ENOMEM;
+        for (size_t st = 0; st < S; st++)
+            for (int t = 0; t < V; t++)
+                if ((bits_host[st * words + (t >> 5)] >> (t & 31)) & 1u)
+                    lm[st * 32 + ((t >> 2) & 31)] |= 1u << (4 * (t >> 7) + (t & 3));
+        cudaError_t e = cudaSuccess;
+        if (!c->allow) e = cudaMalloc(&c->allow, sizeof(uint32_t) * 32 * S);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(c->allow, lm, sizeof(uint32_t) * 32 * S, cudaMemcpyHostToDevice,
+                                c->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+        delete[] lm;
+        if (e != cudaSuccess) return cuda_fail(e, "allow upload");
+    }
     c->allow_on = true;
     return ZONOS2CU_OK;
 }
@@ -491,7 +507,7 @@ int zonos2cu_ctx_sample(zonos2cu_ctx *c, const float *logits_dev, long long row_
     rc = launch_rows(logits_dev, d.n_streams, d.n_cb, d.vocab, row_stride, params, c->rng,
                      c->hist, d.hist_len, c->hist_pos, c->allow_on ? c->allow : nullptr,
                      delay_step, codes_dev, flags_dev, (cudaStream_t)stream, c->counts,
-                     c->presence);
+                     c->presence, /*allow_lane_major*/ true);
     if (rc) return rc;
     if (d.hist_len > 0) c->hist_pos = (c->hist_pos + 1) % d.hist_len;
     return ZONOS2CU_OK;

@@ -6,26 +6,32 @@
 // forcing, non-finite guard), with the row's uniform drawn from a per-stream
 // Xoshiro256** in codebook order (src/zonos2_generate.cpp:259-267).
 //
-// Layout: one CTA per stream, one warp per codebook row.  A row of <= 1024
-// logits lives in 32 registers per lane (lane l, slot 4*j + e holds token
-// 4*(l + 32*j) + e, so every warp load is a coalesced 128-bit access).
+// Two launches per step.  draw_uniforms_kernel (one thread per stream) draws
+// the stream's n_cb uniforms in codebook order, advances its generator and
+// parks each uniform in the row's code slot.  sample_rows_kernel is persistent:
+// every warp walks rows r, r + W, r + 2W, ... (W warps in the grid) on its own,
+// so no warp waits for another; it starts under programmatic dependent launch
+// and waits for the draw grid only before it first reads a uniform.
 //
-// Each warp handles its own row.  After the prologue and the running max, a
-// 128-bucket histogram of the gap (max - l), in buckets T/8 wide (the last one
-// open-ended), finds the bucket B* holding the k-th largest logit.  Buckets
-// <= B*+1 are the candidates: a superset of the top-k that also holds every
-// logit whose probability could round equal to the k-th one's (equal
-// probabilities need logits far closer than a bucket).  In the common case
-// (<= 256 candidates) they are scattered into shared memory in bucket order,
-// get an exact probability, and are put in (p desc, token asc) order by
-// ranking each one inside its bucket; an adjacency check falls back to a
-// bitonic sort if a probability tie straddles a bucket edge.  One running
-// prefix sum of the sorted probabilities serves every sum the reference
-// recomputes from zero, and lane 0 walks the CDFs over quotients p / sum that
-// the warp divides out 32 at a time.  Other rows (top-k off, > 256
-// candidates, degenerate distributions) take a slower general path.  Warp 0
-// draws the stream's uniforms first and hands each codebook's warp its own
-// through a per-warp named barrier.
+// Per row: one bulk copy (TMA) lands the logits in the warp's shared memory
+// and the row a stride ahead is prefetched into L2.  Lane l holds slots
+// 4*(l + 32*j) + e, j < 8, e < 4, so every access is a conflict-free 128-bit
+// one, and a lane-major bitmap (word l, bit 4*j + e) gives a lane all its mask
+// bits in one load; the decode context keeps its history set and allow mask in
+// that layout.  After the prologue and the row max, a 128-bucket histogram of
+// the gap (max - l), in buckets T/8 wide (the last one open-ended), finds the
+// bucket B* holding the k-th largest logit.  Buckets <= B*+1 are the
+// candidates: a superset of the top-k that also holds every logit whose
+// probability could round equal to the k-th one's (equal probabilities need
+// logits far closer than a bucket).  In the common case (<= 256 candidates)
+// they are scattered in bucket order, get an exact probability, and are put in
+// (p desc, token asc) order by ranking each one inside its bucket; an
+// adjacency check falls back to a bitonic sort if a probability tie straddles
+// a bucket edge.  One running prefix sum of the sorted probabilities serves
+// every sum the reference recomputes from zero, and lane 0 walks the CDFs over
+// quotients p / sum that the warp divides out 32 at a time.  Other rows (top-k
+// off, > 256 candidates) take a slower general path; delay-forced rows return
+// the pad token once the row has been checked for non-finite logits.
 //
 // Exactness: every f32 operation that decides the token is the reference's
 // own operation in the reference's order -- (l - max) / T, exp rounded
@@ -37,8 +43,11 @@
 // with RN(1/T) rounded to f32: the f64 error (< 2^-52 relative) cannot reach
 // an f32 rounding boundary, which a quotient of two f32 values never comes
 // closer to than 2^-48 relative, nor hits exactly.  Compiled with -fmad=false:
-// no multiply-add is contracted.
+// no multiply-add is contracted (the one explicit fma places a logit in a
+// bucket, which decides no token).
 #include <math.h>
+
+#include <mutex>
 
 #include "common.cuh"
 #include "cr_exp.h"
@@ -46,35 +55,54 @@
 
 namespace z2 {
 
+__device__ int g_sampler_error = 0;
+
+int read_and_clear_sampler_error(int *value)
+{
+    int v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_sampler_error, sizeof(int));
+    if (e != cudaSuccess) return (int)e;
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_sampler_error, &zero, sizeof(int));
+    if (e != cudaSuccess) return (int)e;
+    *value = v;
+    return 0;
+}
+
 namespace {
 
 // Per-warp shared-memory region (bytes).  Common path:
-//   [0, 2048)      candidates (logit, token), then sorted keys (<= 256 x u64)
-//   [2048, 6144)   the row after the prologue, in token order; then, while
-//                  ranking: unsorted keys [2048, 4096), sorted probabilities
-//                  [4096, 5120), candidate buckets [5120, 5376); while
-//                  deciding: p / sum [2048, 3072), prefix sums [3072, 4096)
-//   [6144, 6656)   2^(j/64), j < 64, for the exp
-//   [6656, 7680)   the bucket byte of every slot
-//   [7680, 8192)   128 bucket counters, then bucket offsets
+//   [0, 4096)      the row: the bulk copy lands the logits, the prologue
+//                  rewrites them in place; free once the candidates are
+//                  compacted (the next row's copy lands here meanwhile)
+//   [4096, 5120)   the bucket byte of every slot (a scanned history's
+//                  seen-bytes during the prologue), then the sorted keys
+//   [5120, 5632)   128 bucket counters, then the sorted probabilities
+//   [5632, 6656)   compacted candidates (logit, token); after the sort the
+//                  prefix sums [5632, 6144) and p / sum [6144, 6656)
 //   [8192, 8320)   1024-bit map of positive tokens (zero-tail fall-through)
-// General path: up to 1024 keys over [0, 8192).  Scan-mode history: the
-// 1024 seen-bytes in [0, 1024) during the prologue.
+//   [8320, 8328)   the row copy's mbarrier
+// General path: up to 1024 keys over [0, 8192) (no copy is in flight then).
 constexpr int kRegion = 8192;
-constexpr int kWarpStride = kRegion + 144;  // + positive map; 16-byte skew between warps
-constexpr int kValOffset = 2048;
-constexpr int kKeyOffset = 2048;
-constexpr int kPsOffset = 4096;
-constexpr int kBucketOffset = 5120;
-constexpr int kQOffset = 2048;
-constexpr int kPfOffset = 3072;
-constexpr int kExpTabOffset = 6144;
-constexpr int kBktOffset = 6656;
-constexpr int kHistOffset = 7680;
+constexpr int kWarpStride = kRegion + 144;
+constexpr int kCtaHeader = 512;          // 2^(j/64), j < 64, shared by the CTA's warps
+constexpr int kRowOffset = 0;
+constexpr int kBktOffset = 4096;
+constexpr int kKeysOffset = 4096;
+constexpr int kHistOffset = 5120;
+constexpr int kPsOffset = 5120;
+constexpr int kStageOffset = 5632;
+constexpr int kPfOffset = 5632;
+constexpr int kQOffset = 6144;
 constexpr int kPosmapOffset = kRegion;
-constexpr int kBuckets = 128;   // gap buckets: 0..126 finite, 127 marks a masked slot
-constexpr int kRankMax = 256;   // candidates handled by the common path
-constexpr int kHeader = 64;     // one uniform per codebook
+constexpr int kBarOffset = kRegion + 128;
+constexpr int kBuckets = 128;    // gap buckets: 0..126 finite, 127 marks a masked slot
+constexpr int kRegSortMax = 128; // candidates sorted in registers (four per lane)
+constexpr int kWarps = 9;       // warps per CTA
+constexpr int kCtasPerSm = 3;   // 27 warps per SM: shared memory and <= 72 registers
+constexpr unsigned long long kWaitNs = 2000000000ull;
+
+enum : int { kErrTimeout = 1 };
 
 __device__ __forceinline__ uint64_t make_key(float p, int tok)
 {
@@ -93,6 +121,10 @@ __device__ __forceinline__ int slot_token(int lane, int i)
 {
     return 4 * (lane + 32 * (i >> 2)) + (i & 3);
 }
+
+// Word and bit of token t in a lane-major 1024-bit map.
+__device__ __forceinline__ int lm_word(int t) { return (t >> 2) & 31; }
+__device__ __forceinline__ uint32_t lm_bit(int t) { return 1u << (4 * (t >> 7) + (t & 3)); }
 
 __device__ __forceinline__ int warp_incl_scan(int x, int lane)
 {
@@ -117,20 +149,23 @@ __device__ __forceinline__ float row_prob(float l, float M, double inv_temp, con
 }
 
 // The build-defined prologue of one logit (slot i of this lane): non-finite
-// guard, repetition penalty, allow / delay mask.
+// guard, repetition penalty (a factor of exactly 1 when the token is unseen),
+// allow / delay mask.
 __device__ __forceinline__ float prologue(float x, int i, uint32_t seenm, uint32_t allowm,
                                           float rho, float inv_rho)
 {
     const bool fin = x < INFINITY;  // false for NaN and +inf
-    if ((seenm >> i) & 1u) x = x * (x > 0.0f ? inv_rho : rho);
-    return (fin && ((allowm >> i) & 1u)) ? x : -INFINITY;
+    const float f = ((seenm >> i) & 1u) ? (x > 0.0f ? inv_rho : rho) : 1.0f;
+    return (fin && ((allowm >> i) & 1u)) ? __fmul_rn(x, f) : -INFINITY;
 }
 
-// Gap bucket of a finite logit, 0..126 (the last one open-ended).  Buckets stay
-// below 128 so that four of them compare against a bound in one subtraction.
-__device__ __forceinline__ int bucket_of(float v, float M, float sc)
+// Gap bucket of a logit, round((max - v) / width) clamped to 126 (the
+// open-ended last bucket), in the low byte of the result; monotone
+// non-increasing in v.  -inf lands in 126.
+__device__ __forceinline__ uint32_t bucket_bits(float v, float sc, float Msc)
 {
-    return (int)fminf((M - v) * sc, (float)(kBuckets - 2));
+    const float t = fminf(__fmaf_rn(-v, sc, Msc), (float)(kBuckets - 2));
+    return __float_as_uint(__fadd_rn(t, 0x1p23f));
 }
 
 // Bit e of the result is set iff byte e of pk is <= bc (bytes and bc < 128).
@@ -145,13 +180,71 @@ __device__ __forceinline__ void mark_seen(unsigned char *seen, int t, int vocab)
     if ((unsigned)t < (unsigned)vocab) seen[t] = 1;
 }
 
-__device__ __forceinline__ void named_arrive(int id, int n)
+// ---- bulk copy, mbarrier, programmatic launch
+__device__ __forceinline__ uint32_t smem_u32(const void *p)
 {
-    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
+    return (uint32_t)__cvta_generic_to_shared(p);
 }
-__device__ __forceinline__ void named_sync(int id, int n)
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count)
 {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// The whole warp waits for the phase with this parity; false (warp-uniform,
+// error word set) after ~2 s.
+__device__ __noinline__ bool mbar_wait_warp_slow(uint32_t bar, uint32_t parity, int lane)
+{
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 1;; it++) {
+        if (__all_sync(kFull, mbar_try_wait(bar, parity))) return true;
+        if ((it & 255u) == 0u &&
+            __shfl_sync(kFull, (int)(globaltimer_ns() - t0 > kWaitNs), 0)) {
+            if (lane == 0) atomicCAS(&g_sampler_error, 0, kErrTimeout);
+            return false;
+        }
+    }
+}
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, int lane)
+{
+    if (__all_sync(kFull, mbar_try_wait(bar, parity))) return true;
+    return mbar_wait_warp_slow(bar, parity, lane);
+}
+// One bulk copy global -> this CTA's shared memory, completing on `bar`
+// (16-byte aligned addresses, size a multiple of 16).
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes,
+                                         uint32_t bar)
+{
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+            "r"(dst), "l"(src), "r"(bytes), "r"(bar)
+        : "memory");
+}
+// Orders this warp's earlier generic accesses to its region before the next
+// bulk copy writes it.
+__device__ __forceinline__ void fence_proxy_async()
+{
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch()
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // Descending bitonic sort of n (power of two, <= 1024) keys in shared memory.
@@ -311,8 +404,7 @@ struct RowKnobs {
 // lane 0.
 __device__ __noinline__ int general_path(const RowKnobs &kn, unsigned char *region,
                                          const float *lrow, uint32_t selm, int n_c, float M,
-                                         uint32_t seenm, uint32_t allowm, int lane, int cb,
-                                         const float *uni)
+                                         uint32_t seenm, uint32_t allowm, int lane, float u)
 {
     uint64_t *ent = reinterpret_cast<uint64_t *>(region);
     __syncwarp();
@@ -399,10 +491,8 @@ __device__ __noinline__ int general_path(const RowKnobs &kn, unsigned char *regi
         if (lane == 0) S = seq_sum(ent, min(n, m));
         S = __shfl_sync(kFull, S, 0);
     }
-    if (cb > 0) named_sync(cb, 64);
     int tok = kn.pad;
     if (lane == 0) {
-        const float u = uni[cb];
         float cum = 0.0f;
         int pos = -1;
         for (int i = 0; i < min(n, m); i++) {
@@ -420,370 +510,459 @@ __device__ __noinline__ int general_path(const RowKnobs &kn, unsigned char *regi
 
 }  // namespace
 
-// MAX_THREADS / MIN_BLOCKS: the 9-codebook model uses <288, 3> (three CTAs,
-// 27 warps per SM at <= 72 registers); wider frames use <512, 1>.
-template <int MAX_THREADS, int MIN_BLOCKS>
-__global__ void __launch_bounds__(MAX_THREADS, MIN_BLOCKS) sample_kernel(const SampleArgs a)
+// One thread per stream: the stream's n_cb uniforms in codebook order, each
+// parked in its row's code slot (as f32 bits) for sample_rows_kernel, and the
+// advanced generator state.
+__global__ void __launch_bounds__(128) draw_uniforms_kernel(uint64_t *rng, int n_streams, int n_cb,
+                                                            uint32_t *slots)
+{
+    grid_dep_launch();   // the sampler may start; it waits for this grid before reading a slot
+    const int s = blockIdx.x * 128 + threadIdx.x;
+    if (s >= n_streams) return;
+    ulonglong2 *sp = reinterpret_cast<ulonglong2 *>(rng + 4 * (size_t)s);
+    const ulonglong2 st01 = sp[0], st23 = sp[1];
+    Xo256 g{st01.x, st01.y, st23.x, st23.y};
+    uint32_t *out = slots + (size_t)s * n_cb;
+    for (int c = 0; c < n_cb; c++) out[c] = __float_as_uint(g.randf());
+    sp[0] = make_ulonglong2(g.s0, g.s1);
+    sp[1] = make_ulonglong2(g.s2, g.s3);
+}
+
+// Descending bitonic sort of 128 keys held four per lane (key e of lane l is
+// element 4*l + e): compare-exchanges inside a lane for distances 1 and 2,
+// shuffles across lanes for the rest.
+__device__ __forceinline__ void cmpx(uint64_t &a, uint64_t &b, bool desc)
+{
+    const bool sw = desc ? (a < b) : (a > b);
+    const uint64_t x = sw ? b : a;
+    const uint64_t y = sw ? a : b;
+    a = x;
+    b = y;
+}
+__device__ __forceinline__ void bitonic128_desc(uint64_t key[4], int lane)
+{
+#pragma unroll 1
+    for (int k = 2; k <= 128; k <<= 1) {
+        const bool desc = ((4 * lane) & k) == 0;   // element 4l + e, k >= 4
+#pragma unroll 1
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            if (j >= 4) {
+                const int lj = j >> 2;
+                const bool keep_max = desc == ((lane & lj) == 0);
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const uint64_t o = __shfl_xor_sync(kFull, key[e], lj);
+                    key[e] = ((key[e] > o) == keep_max) ? key[e] : o;
+                }
+            } else if (j == 2) {
+                cmpx(key[0], key[2], desc);
+                cmpx(key[1], key[3], desc);
+            } else {
+                cmpx(key[0], key[1], k == 2 ? true : desc);
+                cmpx(key[2], key[3], k == 2 ? false : desc);
+            }
+        }
+    }
+}
+
+// Persistent: warp w of CTA b takes work items b + gridDim.x * w + k * W (W warps
+// in the grid).  Items run codebook-major (item cb * n_streams + s is row
+// s * n_cb + cb), so a warp's items cycle through the codebooks whatever the grid,
+// and a row's cost (delay-forced codebooks are cheap) does not stick to one warp.
+// While a row is sorted and decided, the bulk copy of the warp's next row lands.
+__global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(const SampleArgs a)
 {
     extern __shared__ __align__(16) unsigned char smem[];
+    double *exptab = reinterpret_cast<double *>(smem);
     const int lane = threadIdx.x & 31;
-    const int cb = threadIdx.x >> 5;
-    const int s = blockIdx.x;
-    const int V = a.vocab;
-    float *uni = reinterpret_cast<float *>(smem);
-    unsigned char *region = smem + kHeader + cb * kWarpStride;
-    uint64_t *ent = reinterpret_cast<uint64_t *>(region);
+    const int w = threadIdx.x >> 5;
+    unsigned char *region = smem + kCtaHeader + w * kWarpStride;
+    float *rowf = reinterpret_cast<float *>(region + kRowOffset);
     uint32_t *hist = reinterpret_cast<uint32_t *>(region + kHistOffset);
     uint32_t *bkt = reinterpret_cast<uint32_t *>(region + kBktOffset);
-    double *exptab = reinterpret_cast<double *>(region + kExpTabOffset);
-    const size_t row = (size_t)s * (size_t)a.n_cb + (size_t)cb;
+    const uint32_t bar = smem_u32(region + kBarOffset);
+    if (threadIdx.x < 64) exptab[threadIdx.x] = exp2_64th(threadIdx.x);
+    if (lane == 0) {
+        mbar_init(bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    const int V = a.vocab;
+    const int NCB = a.n_cb;
+    const int S_ = a.n_streams;
     const int K = a.top_k;
     const bool topk_on = K > 0 && K < V;
+    const bool pen = a.hist_len > 0 && a.rho != 1.0f;
+    const bool inc = a.presence != nullptr;
+    const uint32_t row_bytes = 4u * (uint32_t)V;
+    const uint32_t *slots = reinterpret_cast<const uint32_t *>(a.codes);
+    RowKnobs kn;
+    kn.V = V;
+    kn.K = K;
+    kn.topk_on = topk_on;
+    kn.top_p = a.top_p;
+    kn.min_p = a.min_p;
+    kn.rho = a.rho;
+    kn.inv_rho = a.inv_rho;
+    kn.inv_temp = a.inv_temp;
+    kn.pad = a.pad_id;
 
-    // ---- 1. the logits row -> registers; the exp table -> shared memory
-    float v[32];
-    const float *lrow = a.logits + row * (size_t)a.row_stride;
-    if (a.vec_logits) {
+    // work items: (s, cb) of item it, advanced by the grid's warp count
+    const long long step = (long long)gridDim.x * kWarps;
+    const int step_cb = (int)(step / S_);
+    const int step_s = (int)(step - (long long)step_cb * S_);
+    const long long it0 = blockIdx.x + (long long)gridDim.x * w;
+    int cb = (int)(it0 / S_);
+    int s = (int)(it0 - (long long)cb * S_);
+
+    uint32_t phase = 0u;
+    bool drawn = false;     // the draw grid has been waited for
+    bool pending = false;   // the copy of the current row is in flight
+    uint32_t seen_next = 0u, allow_next = ~0u;   // lane-major masks of the next row
+
+    // Starts the bulk copy of row (s2, cb2) and loads its lane-major masks.
+    auto issue = [&](int s2, int cb2) {
+        const long long r2 = (long long)s2 * NCB + cb2;
+        if (a.vec_logits && lane == 0) {
+            fence_proxy_async();
+            mbar_expect_tx(bar, row_bytes);
+            bulk_g2s(smem_u32(rowf), a.logits + r2 * a.row_stride, row_bytes, bar);
+        }
+        if (pen && inc) seen_next = __ldcg(a.presence + (size_t)r2 * 32 + lane);
+        if (a.allow && a.allow_lane_major) allow_next = __ldg(a.allow + (size_t)s2 * 32 + lane);
+        pending = true;
+    };
+    if (cb < NCB) issue(s, cb);
+
+    while (cb < NCB) {
+        const long long r = (long long)s * NCB + cb;
+        const float *lrow = a.logits + r * a.row_stride;
+        int s_nx = s + step_s, cb_nx = cb + step_cb;
+        if (s_nx >= S_) {
+            s_nx -= S_;
+            cb_nx++;
+        }
+        if (!pending) issue(s, cb);
+
+        // ---- 1. the history's token set and the allow bits
+        uint32_t seenm = seen_next, allowm = ~0u;
+        if (pen && !inc) {   // scan the ring into seen-bytes
+            unsigned char *seen = region + kBktOffset;
+            uint4 *seen4 = reinterpret_cast<uint4 *>(seen);
+            seen4[2 * lane] = make_uint4(0u, 0u, 0u, 0u);
+            seen4[2 * lane + 1] = make_uint4(0u, 0u, 0u, 0u);
+            __syncwarp();
+            const int32_t *hrow = a.hist + (size_t)r * a.hist_len;
+            const int H = a.hist_len;
+            if (a.vec_hist) {
+                for (int q0 = 0; q0 < H; q0 += 512) {
+                    int4 t[4];
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        const int q = q0 + 4 * lane + 128 * u;
+                        t[u] = q < H ? __ldcg(reinterpret_cast<const int4 *>(hrow + q))
+                                     : make_int4(-1, -1, -1, -1);
+                    }
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        mark_seen(seen, t[u].x, V);
+                        mark_seen(seen, t[u].y, V);
+                        mark_seen(seen, t[u].z, V);
+                        mark_seen(seen, t[u].w, V);
+                    }
+                }
+            } else {
+                for (int q = lane; q < H; q += 32) mark_seen(seen, __ldcg(hrow + q), V);
+            }
+            __syncwarp();
+            seenm = 0u;
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const uint32_t wd = *reinterpret_cast<const uint32_t *>(seen + 4 * (lane + 32 * j));
+                seenm |= ((wd * 0x10204080u) >> 28) << (4 * j);   // four 0/1 bytes -> 4 bits
+            }
+        }
+        if (a.allow) {
+            if (a.allow_lane_major) {
+                allowm = allow_next;
+            } else {
+                const uint32_t aw = lane < a.allow_words
+                                        ? __ldg(a.allow + (size_t)s * a.allow_words + lane)
+                                        : ~0u;
+                allowm = 0u;
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const uint32_t wv = __shfl_sync(kFull, aw, (lane + 32 * j) >> 3);
+                    allowm |= ((wv >> (4 * (lane & 7))) & 0xfu) << (4 * j);
+                }
+            }
+        }
+        const bool forced = a.delay_step >= 0 && a.delay_step < cb;
+        if (forced) {   // delay pattern: only the pad token
+            const int p = a.pad_id;
+            allowm &= lane == ((p >> 2) & 31) ? lm_bit(p) : 0u;
+        }
+
+        // ---- 2. wait for the row; slots -> registers
+        if (a.vec_logits) {
+            if (!mbar_wait_warp(bar, phase, lane)) return;   // the error word is set
+            phase ^= 1u;
+        } else {
+            for (int t = lane; t < ((V + 3) & ~3); t += 32)
+                rowf[t] = t < V ? __ldg(lrow + t) : -INFINITY;
+            __syncwarp();
+        }
+        pending = false;
+        float v[32];
 #pragma unroll
         for (int j = 0; j < 8; j++) {
             const int t0 = 4 * (lane + 32 * j);
             float4 f = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-            if (t0 < V) f = __ldg(reinterpret_cast<const float4 *>(lrow + t0));
+            if (t0 < V) f = *reinterpret_cast<const float4 *>(rowf + t0);
             v[4 * j + 0] = f.x;
             v[4 * j + 1] = f.y;
             v[4 * j + 2] = f.z;
             v[4 * j + 3] = f.w;
         }
-    } else {
-#pragma unroll
-        for (int j = 0; j < 8; j++)
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const int t = 4 * (lane + 32 * j) + e;
-                v[4 * j + e] = t < V ? __ldg(lrow + t) : -INFINITY;
-            }
-    }
-    exptab[lane] = exp2_64th(lane);
-    exptab[lane + 32] = exp2_64th(lane + 32);
 
-    // ---- 2. the stream's uniforms: warp 0 draws one per codebook, in codebook
-    // order, and releases codebook c's warp through named barrier c
-    if (cb == 0) {
-        if (lane == 0) {
-            ulonglong2 *sp = reinterpret_cast<ulonglong2 *>(a.rng + 4 * (size_t)s);
-            const ulonglong2 st01 = sp[0], st23 = sp[1];
-            Xo256 g{st01.x, st01.y, st23.x, st23.y};
-            for (int c = 0; c < a.n_cb; c++) uni[c] = g.randf();
-            sp[0] = make_ulonglong2(g.s0, g.s1);
-            sp[1] = make_ulonglong2(g.s2, g.s3);
-            __threadfence_block();
+        // ---- 3. prologue and row max; the row is rewritten in place
+        bool nonfin = false;
+        float mx = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+            nonfin |= !(v[i] < INFINITY);
+            v[i] = prologue(v[i], i, seenm, allowm, a.rho, a.inv_rho);
+            mx = fmaxf(mx, v[i]);
         }
-        __syncwarp();
-        for (int c = 1; c < a.n_cb; c++) named_arrive(c, 64);
-    }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+        const bool live = mx >= -1e9f;  // running max starts at -1e9: :41-42
+        const int flag = (__any_sync(kFull, nonfin) ? 2 : 0) | (live ? 0 : 1);
 
-    // ---- 3. the history's token set: the context keeps it as a bitmap;
-    // otherwise the ring is scanned into seen-bytes
-    const bool pen = a.hist_len > 0 && a.rho != 1.0f;
-    const bool inc = a.presence != nullptr;
-    uint32_t seenm = 0u, allowm = ~0u;
-    if (pen && inc) {
-        const uint32_t pw = lane < a.allow_words
-                                ? __ldcg(a.presence + row * (size_t)a.allow_words + lane)
-                                : 0u;
+        int tok = a.pad_id;
+        if (live && !forced) {
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const uint32_t w = __shfl_sync(kFull, pw, (lane + 32 * j) >> 3);
-            seenm |= ((w >> (4 * (lane & 7))) & 0xfu) << (4 * j);
-        }
-    } else if (pen) {
-        uint4 *seen4 = reinterpret_cast<uint4 *>(region);
-        seen4[2 * lane] = make_uint4(0u, 0u, 0u, 0u);
-        seen4[2 * lane + 1] = make_uint4(0u, 0u, 0u, 0u);
-        __syncwarp();
-        const int32_t *hrow = a.hist + row * (size_t)a.hist_len;
-        const int H = a.hist_len;
-        if (a.vec_hist) {
-            for (int q0 = 0; q0 < H; q0 += 512) {
-                int4 t[4];
+            for (int j = 0; j < 8; j++)
+                *reinterpret_cast<float4 *>(rowf + 4 * (lane + 32 * j)) =
+                    make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            const float M = mx;
+            const float T = a.temperature;
+            // ---- 4. gap histogram and the bucket of the k-th largest logit.  The
+            // open-ended last bucket holds most of a row: it is not counted with
+            // atomics, its count follows from the number of finite logits.
+            const float bw = fmaxf(T * 0.125f, fabsf(M) * 0x1p-18f + T * 0x1p-14f);
+            const float sc = 1.0f / bw;
+            const float Msc = M * sc;
+            reinterpret_cast<uint4 *>(hist)[lane] = make_uint4(0u, 0u, 0u, 0u);
+            __syncwarp();
+            int nf = 0;
 #pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    const int q = q0 + 4 * lane + 128 * u;
-                    t[u] = q < H ? __ldcg(reinterpret_cast<const int4 *>(hrow + q))
-                                 : make_int4(-1, -1, -1, -1);
+            for (int j = 0; j < 8; j++) {
+                uint32_t bb[4];
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const float x = v[4 * j + e];
+                    const bool fin = x > -INFINITY;
+                    const uint32_t bits = bucket_bits(x, sc, Msc);
+                    const uint32_t b = bits & 0x7fu;
+                    if (b < (uint32_t)(kBuckets - 2)) atomicAdd(hist + b, 1u);  // -inf: 126
+                    nf += fin;
+                    bb[e] = fin ? bits : (uint32_t)(kBuckets - 1);
                 }
-#pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    mark_seen(region, t[u].x, V);
-                    mark_seen(region, t[u].y, V);
-                    mark_seen(region, t[u].z, V);
-                    mark_seen(region, t[u].w, V);
-                }
+                bkt[lane + 32 * j] = __byte_perm(__byte_perm(bb[0], bb[1], 0x0040u),
+                                                 __byte_perm(bb[2], bb[3], 0x0040u), 0x5410u);
             }
-        } else {
-            for (int q = lane; q < H; q += 32) mark_seen(region, __ldcg(hrow + q), V);
-        }
-        __syncwarp();
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const uint32_t wd = *reinterpret_cast<const uint32_t *>(region + 4 * (lane + 32 * j));
-            seenm |= ((wd * 0x10204080u) >> 28) << (4 * j);   // four 0/1 bytes -> 4 bits
-        }
-    }
-
-    // ---- 4. prologue: penalty, allow bits, delay forcing, non-finite guard
-    if (a.allow) {
-        const uint32_t aw = lane < a.allow_words ? __ldg(a.allow + (size_t)s * a.allow_words + lane)
-                                                 : ~0u;
-        allowm = 0u;
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const uint32_t w = __shfl_sync(kFull, aw, (lane + 32 * j) >> 3);
-            allowm |= ((w >> (4 * (lane & 7))) & 0xfu) << (4 * j);
-        }
-    }
-    if (a.delay_step >= 0 && a.delay_step < cb) {  // delay pattern: only the pad token
-        const int p = a.pad_id;
-        allowm &= lane == ((p >> 2) & 31) ? (1u << (4 * (p >> 7) + (p & 3))) : 0u;
-    }
-    bool nonfin = false;
-    float mx = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < 32; i++) {
-        nonfin |= !(v[i] < INFINITY);
-        v[i] = prologue(v[i], i, seenm, allowm, a.rho, a.inv_rho);
-        mx = fmaxf(mx, v[i]);
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
-    const bool live = mx >= -1e9f;  // running max starts at -1e9: :41-42
-    const int flag = (__any_sync(kFull, nonfin) ? 2 : 0) | (live ? 0 : 1);
-    {   // keep the row for the candidate scatter (the registers die after the histogram)
-        float4 *vs = reinterpret_cast<float4 *>(region + kValOffset);
-#pragma unroll
-        for (int j = 0; j < 8; j++)
-            vs[lane + 32 * j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-    }
-
-    int tok = a.pad_id;
-    if (live) {
-        const float M = mx;
-        const float T = a.temperature;
-        // ---- 5. gap histogram and the bucket of the k-th largest logit.  The
-        // open-ended last bucket holds most of a row: it is not counted with
-        // atomics, its count follows from the number of finite logits.
-        const float bw = fmaxf(T * 0.125f, fabsf(M) * 0x1p-18f + T * 0x1p-14f);
-        const float sc = 1.0f / bw;
-        reinterpret_cast<uint4 *>(hist)[lane] = make_uint4(0u, 0u, 0u, 0u);
-        __syncwarp();
-        int nf = 0;
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-            uint32_t pk = 0u;
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const float x = v[4 * j + e];
-                const bool fin = x > -INFINITY;
-                const int b = bucket_of(x, M, sc);
-                if (fin && b < kBuckets - 2) atomicAdd(hist + b, 1u);
-                nf += fin;
-                pk |= (uint32_t)(fin ? b : kBuckets - 1) << (8 * e);
+            const int n_fin = __reduce_add_sync(kFull, nf);
+            __syncwarp();
+            const uint4 h4 = reinterpret_cast<const uint4 *>(hist)[lane];
+            int h[4] = {(int)h4.x, (int)h4.y, (int)h4.z, (int)h4.w};
+            int tot = h[0] + h[1] + h[2] + h[3];
+            int incl = warp_incl_scan(tot, lane);
+            if (lane == 31) {   // bucket 126 = 4*31 + 2
+                const int rest = n_fin - incl;
+                h[2] += rest;
+                tot += rest;
+                incl += rest;
             }
-            bkt[lane + 32 * j] = pk;
-        }
-        const int n_fin = __reduce_add_sync(kFull, nf);
-        __syncwarp();
-        const uint4 h4 = reinterpret_cast<const uint4 *>(hist)[lane];
-        int h[4] = {(int)h4.x, (int)h4.y, (int)h4.z, (int)h4.w};
-        int tot = h[0] + h[1] + h[2] + h[3];
-        int incl = warp_incl_scan(tot, lane);
-        if (lane == 31) {   // bucket 126 = 4*31 + 2
-            const int rest = n_fin - incl;
-            h[2] += rest;
-            tot += rest;
-            incl += rest;
-        }
-        int bc = kBuckets - 2;   // every finite logit
-        if (topk_on && n_fin > K) {
-            const int fl = __ffs(__ballot_sync(kFull, incl >= K)) - 1;
-            int bstar = 0;
-            if (lane == fl) {
-                int c = incl - tot;
+            int bc = kBuckets - 2;   // every finite logit
+            if (topk_on && n_fin > K) {
+                const int fl = __ffs(__ballot_sync(kFull, incl >= K)) - 1;
+                int bstar = 0;
+                if (lane == fl) {
+                    int c = incl - tot;
 #pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    c += h[i];
-                    if (c >= K) {
-                        bstar = 4 * lane + i;
-                        break;
+                    for (int i = 0; i < 4; i++) {
+                        c += h[i];
+                        if (c >= K) {
+                            bstar = 4 * lane + i;
+                            break;
+                        }
                     }
                 }
+                bc = min(__shfl_sync(kFull, bstar, fl) + 1, kBuckets - 2);
             }
-            bc = min(__shfl_sync(kFull, bstar, fl) + 1, kBuckets - 2);
-        }
-        int n_c;   // candidates: finite logits in buckets 0..bc
-        {
-            int c = incl - tot, upto = 0;
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                if (4 * lane + i == bc) upto = c + h[i];
-                c += h[i];
-            }
-            n_c = __shfl_sync(kFull, upto, bc >> 2);
-        }
-        const uint32_t bc4 = 0x80808080u | ((uint32_t)bc * 0x01010101u);
-        uint32_t selm = 0u;   // this lane's candidate slots
-#pragma unroll
-        for (int j = 0; j < 8; j++) selm |= bytes_le(bkt[lane + 32 * j], bc4) << (4 * j);
-
-        RowKnobs kn;
-        kn.V = V;
-        kn.K = K;
-        kn.topk_on = topk_on;
-        kn.top_p = a.top_p;
-        kn.min_p = a.min_p;
-        kn.rho = a.rho;
-        kn.inv_rho = a.inv_rho;
-        kn.inv_temp = a.inv_temp;
-        kn.pad = a.pad_id;
-        if (!topk_on || n_c > kRankMax) {
-            tok = general_path(kn, region, lrow, selm, n_c, M, seenm, allowm, lane, cb, uni);
-        } else {
-            // ---- 6. candidates -> shared memory in bucket order, from the row copy
+            int n_c;   // candidates: finite logits in buckets 0..bc
             {
-                const int c0 = incl - tot;
-                reinterpret_cast<uint4 *>(hist)[lane] =
-                    make_uint4(c0, c0 + h[0], c0 + h[0] + h[1], c0 + h[0] + h[1] + h[2]);
-                __syncwarp();
-            }
-            const float *vs = reinterpret_cast<const float *>(region + kValOffset);
-            uint32_t sm = selm;
-            while (sm) {
-                const int i = __ffs(sm) - 1;
-                sm &= sm - 1;
-                const int t = slot_token(lane, i);
-                const int b = (bkt[lane + 32 * (i >> 2)] >> (8 * (i & 3))) & 0xff;
-                const int pos = atomicAdd(hist + b, 1u);
-                ent[pos] = make_ent(vs[t], t);
-            }
-            __syncwarp();
-
-            // ---- 7. exact probabilities (src/zonos2_generate.cpp:44-49), keys
-            // ranked inside their buckets
-            const SmemExpTable tab{exptab};
-            uint64_t *k2 = reinterpret_cast<uint64_t *>(region + kKeyOffset);
-            unsigned char *kb = region + kBucketOffset;
-            float *ps = reinterpret_cast<float *>(region + kPsOffset);
-            int np = 0;
-#pragma unroll 2
-            for (int q = lane; q < n_c; q += 32) {
-                const uint64_t en = ent[q];
-                const float x = ent_v(en);
-                const float p = row_prob(x, M, a.inv_temp, tab);
-                np += p > 0.0f;
-                k2[q] = make_key(p, (int)(uint32_t)en);
-                kb[q] = (unsigned char)bucket_of(x, M, sc);
-            }
-            const int n_pos = __reduce_add_sync(kFull, np);
-            __syncwarp();
-#pragma unroll 2
-            for (int q = lane; q < n_c; q += 32) {
-                const uint64_t key = k2[q];
-                const int b = kb[q];
-                const int lo = b ? (int)hist[b - 1] : 0;
-                const int hi = (int)hist[b];
-                int rank = 0, i = lo;
-                for (; i + 2 <= hi; i += 2) rank += (k2[i] > key) + (k2[i + 1] > key);
-                if (i < hi) rank += k2[i] > key;
-                ent[lo + rank] = key;
-                ps[lo + rank] = key_p(key);
-            }
-            __syncwarp();
-            bool bad = false;
-            for (int q = lane; q + 1 < n_c; q += 32) bad |= ent[q] < ent[q + 1];
-            if (__any_sync(kFull, bad)) {   // a probability tie across a bucket edge
-                int N = 32;
-                while (N < n_c) N <<= 1;
-                for (int i = n_c + lane; i < N; i += 32) ent[i] = 0ull;
-                __syncwarp();
-                bitonic_smem_desc(ent, N, lane);
-                for (int q = lane; q < n_c; q += 32) ps[q] = key_p(ent[q]);
-                __syncwarp();
-            }
-
-            // ---- 8. top-k / top-p / min-p (src/zonos2_generate.cpp:55-84).  The
-            // list is ent[0..m) (positive probabilities, sorted) followed by
-            // zero-probability tokens in token order, n entries in all; every sum
-            // the reference recomputes from zero over a sorted prefix is one of
-            // the running prefix sums.
-            const int m = min(n_pos, K);
-            int n = K;
-            float *pf = reinterpret_cast<float *>(region + kPfOffset);
-            float *q = reinterpret_cast<float *>(region + kQOffset);
-            if (lane == 0) prefix_sums(ps, pf, m);
-            __syncwarp();
-            float S = pf[m - 1];
-            if (a.top_p < 1.0f) {
-                const int cut = walk_cdf(ps, q, m, S, a.top_p, lane);
-                if (cut > 0) n = cut;  // never inside the zero tail: the sum stops growing
-                S = pf[min(n, m) - 1];
-            }
-            if (a.min_p > 0.0f) {
-                const float thresh = (ps[0] / S) * a.min_p;
-                const int mm = min(n, m);
-                int j = minp_cut(ps, mm, S, thresh, lane);
-                if (j == mm && n > mm) j = (0.0f >= thresh) ? n : mm;
-                n = j;
-                S = pf[min(n, m) - 1];
-            }
-            if (cb > 0) named_sync(cb, 64);   // this codebook's uniform is in shared memory
-            // ---- 9. one uniform, CDF walk (src/zonos2_generate.cpp:86-92)
-            const int hit = walk_cdf(ps, q, min(n, m), S, uni[cb], lane);
-            if (lane == 0)
-                tok = pick_token(ent, hit > 0 ? hit - 1 : -1, n, m, n_pos,
-                                 reinterpret_cast<uint32_t *>(region + kPosmapOffset), V,
-                                 a.pad_id);
-        }
-    } else if (cb > 0) {
-        named_sync(cb, 64);
-    }
-
-    if (lane == 0) {
-        a.codes[row] = tok;
-        if (a.flags) a.flags[row] = flag;
-        if (a.hist && a.hist_len > 0) {
-            int32_t *ring = a.hist + row * (size_t)a.hist_len;
-            if (inc) {   // the evicted token leaves the index, the new one enters
-                const int ev = __ldcg(ring + a.hist_pos);
-                uint16_t *cnt = a.counts + row * (size_t)V;
-                uint32_t *pm = a.presence + row * (size_t)a.allow_words;
-                if ((unsigned)ev < (unsigned)V) {
-                    const unsigned c = cnt[ev] - 1u;
-                    cnt[ev] = (uint16_t)c;
-                    if (c == 0u) pm[ev >> 5] &= ~(1u << (ev & 31));
+                int c = incl - tot, upto = 0;
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    if (4 * lane + i == bc) upto = c + h[i];
+                    c += h[i];
                 }
-                if ((unsigned)tok < (unsigned)V) {
-                    const unsigned c = cnt[tok];
-                    cnt[tok] = (uint16_t)(c + 1u);
-                    if (c == 0u) pm[tok >> 5] |= 1u << (tok & 31);
-                }
+                n_c = __shfl_sync(kFull, upto, bc >> 2);
             }
-            ring[a.hist_pos] = tok;
+            const uint32_t bc4 = 0x80808080u | ((uint32_t)bc * 0x01010101u);
+            uint32_t selm = 0u;   // this lane's candidate slots
+#pragma unroll
+            for (int j = 0; j < 8; j++) selm |= bytes_le(bkt[lane + 32 * j], bc4) << (4 * j);
+
+            // the uniform: its producer has finished once waited for
+            if (!drawn) {
+                grid_dep_wait();
+                drawn = true;
+            }
+            const float u = __uint_as_float(__ldcg(slots + r));
+
+            if (!topk_on || n_c > kRegSortMax) {
+                tok = general_path(kn, region, lrow, selm, n_c, M, seenm, allowm, lane, u);
+                __syncwarp();
+                if (cb_nx < NCB) issue(s_nx, cb_nx);
+            } else {
+                // ---- 5. candidates -> four per lane (compaction through shared memory)
+                uint64_t *stage = reinterpret_cast<uint64_t *>(region + kStageOffset);
+                {
+                    const int cnt = __popc(selm);
+                    int pos = warp_incl_scan(cnt, lane) - cnt;
+                    uint32_t sm = selm;
+                    while (sm) {
+                        const int i = __ffs(sm) - 1;
+                        sm &= sm - 1;
+                        const int t = slot_token(lane, i);
+                        stage[pos++] = make_ent(rowf[t], t);
+                    }
+                }
+                __syncwarp();
+                uint64_t key[4];
+                {
+                    const ulonglong2 e01 = reinterpret_cast<const ulonglong2 *>(stage)[2 * lane];
+                    const ulonglong2 e23 = reinterpret_cast<const ulonglong2 *>(stage)[2 * lane + 1];
+                    key[0] = e01.x;
+                    key[1] = e01.y;
+                    key[2] = e23.x;
+                    key[3] = e23.y;
+                }
+                __syncwarp();   // the row and the stage are free
+                if (cb_nx < NCB) issue(s_nx, cb_nx);
+
+                // ---- 6. exact probabilities (src/zonos2_generate.cpp:44-49) and the
+                // (p desc, token asc) order of the candidates
+                const SmemExpTable tab{exptab};
+                int np = 0;
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    if (4 * lane + e < n_c) {
+                        const float p = row_prob(ent_v(key[e]), M, a.inv_temp, tab);
+                        np += p > 0.0f;
+                        key[e] = make_key(p, (int)(uint32_t)key[e]);
+                    } else {
+                        key[e] = 0ull;   // sorts after every candidate
+                    }
+                }
+                const int n_pos = __reduce_add_sync(kFull, np);
+                bitonic128_desc(key, lane);
+                uint64_t *keys = reinterpret_cast<uint64_t *>(region + kKeysOffset);
+                float *ps = reinterpret_cast<float *>(region + kPsOffset);
+                reinterpret_cast<ulonglong2 *>(keys)[2 * lane] = make_ulonglong2(key[0], key[1]);
+                reinterpret_cast<ulonglong2 *>(keys)[2 * lane + 1] = make_ulonglong2(key[2], key[3]);
+                reinterpret_cast<float4 *>(ps)[lane] =
+                    make_float4(key_p(key[0]), key_p(key[1]), key_p(key[2]), key_p(key[3]));
+                __syncwarp();
+
+                // ---- 7. top-k / top-p / min-p (src/zonos2_generate.cpp:55-84).  The
+                // list is keys[0..m) (positive probabilities, sorted) followed by
+                // zero-probability tokens in token order, n entries in all; every sum
+                // the reference recomputes from zero over a sorted prefix is one of
+                // the running prefix sums.
+                const int m = min(n_pos, K);
+                int n = K;
+                float *pf = reinterpret_cast<float *>(region + kPfOffset);
+                float *q = reinterpret_cast<float *>(region + kQOffset);
+                if (lane == 0) prefix_sums(ps, pf, m);
+                __syncwarp();
+                float S = pf[m - 1];
+                if (a.top_p < 1.0f) {
+                    const int cut = walk_cdf(ps, q, m, S, a.top_p, lane);
+                    if (cut > 0) n = cut;  // never inside the zero tail: the sum stops growing
+                    S = pf[min(n, m) - 1];
+                }
+                if (a.min_p > 0.0f) {
+                    const float thresh = (ps[0] / S) * a.min_p;
+                    const int mm = min(n, m);
+                    int j = minp_cut(ps, mm, S, thresh, lane);
+                    if (j == mm && n > mm) j = (0.0f >= thresh) ? n : mm;
+                    n = j;
+                    S = pf[min(n, m) - 1];
+                }
+                // ---- 8. one uniform, CDF walk (src/zonos2_generate.cpp:86-92)
+                const int hit = walk_cdf(ps, q, min(n, m), S, u, lane);
+                if (lane == 0)
+                    tok = pick_token(keys, hit > 0 ? hit - 1 : -1, n, m, n_pos,
+                                     reinterpret_cast<uint32_t *>(region + kPosmapOffset), V,
+                                     a.pad_id);
+            }
+        } else {
+            __syncwarp();   // the row is free
+            if (cb_nx < NCB) issue(s_nx, cb_nx);
         }
+
+        // ---- 9. the code (over its parked uniform), flag and history
+        if (!drawn) {
+            grid_dep_wait();
+            drawn = true;
+        }
+        if (lane == 0) {
+            a.codes[r] = tok;
+            if (a.flags) a.flags[r] = flag;
+            if (a.hist && a.hist_len > 0) {
+                int32_t *ring = a.hist + (size_t)r * a.hist_len;
+                if (inc) {   // the evicted token leaves the index, the new one enters
+                    const int ev = __ldcg(ring + a.hist_pos);
+                    uint16_t *cnt = a.counts + (size_t)r * V;
+                    uint32_t *pm = a.presence + (size_t)r * 32;
+                    if ((unsigned)ev < (unsigned)V) {
+                        const unsigned c = cnt[ev] - 1u;
+                        cnt[ev] = (uint16_t)c;
+                        if (c == 0u) pm[lm_word(ev)] &= ~lm_bit(ev);
+                    }
+                    if ((unsigned)tok < (unsigned)V) {
+                        const unsigned c = cnt[tok];
+                        cnt[tok] = (uint16_t)(c + 1u);
+                        if (c == 0u) pm[lm_word(tok)] |= lm_bit(tok);
+                    }
+                }
+                ring[a.hist_pos] = tok;
+            }
+        }
+        __syncwarp();
+        s = s_nx;
+        cb = cb_nx;
     }
 }
 
 // One warp per history ring: token counts in shared memory, then the u16
-// counts and the presence bitmap.
+// counts and the lane-major presence bitmap (word l, bit 4*j + e: token
+// 4*(l + 32*j) + e).
 __global__ void __launch_bounds__(256) history_index_kernel(const int32_t *hist, long long rows,
-                                                            int H, int V, int words,
-                                                            uint16_t *counts, uint32_t *presence)
+                                                            int H, int V, uint16_t *counts,
+                                                            uint32_t *presence)
 {
     __shared__ uint32_t c[8][kSamplerVocabMax];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const long long row = (long long)blockIdx.x * 8 + w;
     if (row >= rows) return;
     uint32_t *cw = c[w];
-    for (int t = lane; t < V; t += 32) cw[t] = 0u;
+    for (int t = lane; t < kSamplerVocabMax; t += 32) cw[t] = 0u;
     __syncwarp();
     const int32_t *ring = hist + row * (size_t)H;
     for (int q = lane; q < H; q += 32) {
@@ -792,53 +971,85 @@ __global__ void __launch_bounds__(256) history_index_kernel(const int32_t *hist,
     }
     __syncwarp();
     for (int t = lane; t < V; t += 32) counts[row * (size_t)V + t] = (uint16_t)cw[t];
-    for (int wd = 0; wd < words; wd++) {
-        const int t = 32 * wd + lane;
-        const uint32_t bits = __ballot_sync(kFull, t < V && cw[t] > 0u);
-        if (lane == 0) presence[row * (size_t)words + wd] = bits;
-    }
+    uint32_t bits = 0u;
+#pragma unroll
+    for (int i = 0; i < 32; i++) bits |= (cw[slot_token(lane, i)] > 0u ? 1u : 0u) << i;
+    presence[row * 32 + lane] = bits;
 }
 
 cudaError_t launch_history_index(const int32_t *hist, long long rows, int hist_len, int vocab,
                                  uint16_t *counts, uint32_t *presence, cudaStream_t stream)
 {
     if (rows == 0) return cudaSuccess;
-    const int words = (vocab + 31) / 32;
-    history_index_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, stream>>>(
-        hist, rows, hist_len, vocab, words, counts, presence);
+    history_index_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, stream>>>(hist, rows, hist_len,
+                                                                         vocab, counts, presence);
     return cudaGetLastError();
 }
 
-size_t sample_smem_bytes(int n_cb) { return (size_t)kHeader + (size_t)n_cb * kWarpStride; }
+size_t sample_smem_bytes() { return (size_t)kCtaHeader + (size_t)kWarps * kWarpStride; }
 
-template <int MAX_THREADS, int MIN_BLOCKS>
-static cudaError_t launch_variant(const SampleArgs &a, cudaStream_t stream, bool *attr_done)
+namespace {
+
+struct DeviceLaunchInfo {
+    bool ready = false;
+    int grid_cap = 0;   // resident CTAs of the sampler on this device
+};
+std::mutex g_launch_mu;
+DeviceLaunchInfo g_launch_info[64];
+
+cudaError_t launch_info(int dev, int *grid_cap)
 {
-    const int max_cb = MAX_THREADS / 32;
-    if (!*attr_done) {
-        const cudaError_t e =
-            cudaFuncSetAttribute(sample_kernel<MAX_THREADS, MIN_BLOCKS>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)sample_smem_bytes(max_cb));
+    std::lock_guard<std::mutex> lk(g_launch_mu);
+    DeviceLaunchInfo &d = g_launch_info[dev];
+    if (!d.ready) {
+        cudaError_t e = cudaFuncSetAttribute(sample_rows_kernel,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)sample_smem_bytes());
         if (e != cudaSuccess) return e;
-        *attr_done = true;
+        int sms = 0, per_sm = 0;
+        e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sample_rows_kernel,
+                                                          32 * kWarps, sample_smem_bytes());
+        if (e != cudaSuccess) return e;
+        d.grid_cap = sms * (per_sm > 0 ? per_sm : 1);
+        d.ready = true;
     }
-    sample_kernel<MAX_THREADS, MIN_BLOCKS>
-        <<<a.n_streams, 32 * a.n_cb, sample_smem_bytes(a.n_cb), stream>>>(a);
-    return cudaGetLastError();
+    *grid_cap = d.grid_cap;
+    return cudaSuccess;
 }
+
+}  // namespace
 
 cudaError_t launch_sample(const SampleArgs &a, cudaStream_t stream)
 {
     if (a.n_streams == 0) return cudaSuccess;
     int dev = 0;
-    const cudaError_t e = cudaGetDevice(&dev);
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    static bool attr_narrow[64] = {false};
-    static bool attr_wide[64] = {false};
-    if (a.n_cb <= 9) return launch_variant<288, 3>(a, stream, &attr_narrow[dev]);
-    return launch_variant<32 * kSamplerCbMax, 1>(a, stream, &attr_wide[dev]);
+    int cap = 0;
+    e = launch_info(dev, &cap);
+    if (e != cudaSuccess) return e;
+
+    draw_uniforms_kernel<<<(unsigned)((a.n_streams + 127) / 128), 128, 0, stream>>>(
+        a.rng, a.n_streams, a.n_cb, reinterpret_cast<uint32_t *>(a.codes));
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+
+    const long long rows = (long long)a.n_streams * a.n_cb;
+    const long long need = (rows + kWarps - 1) / kWarps;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(need < cap ? need : cap));
+    cfg.blockDim = dim3(32 * kWarps);
+    cfg.dynamicSmemBytes = sample_smem_bytes();
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, sample_rows_kernel, a);
 }
 
 }  // namespace z2

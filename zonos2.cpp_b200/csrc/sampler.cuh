@@ -19,10 +19,13 @@ struct SampleArgs {
     uint64_t *rng;           // [n_streams][4]
     int32_t *hist;           // [n_streams][n_cb][hist_len] or nullptr
     int hist_len, hist_pos;
-    const uint32_t *allow;   // [n_streams][allow_words] or nullptr
+    const uint32_t *allow;   // [n_streams][allow_words] or, lane-major, [n_streams][32]
     int allow_words;
+    int allow_lane_major;    // allow holds lane-major words (word l, bit 4*j + e: token
+                             // 4*(l + 32*j) + e), 32 per stream
     int delay_step;
-    int32_t *codes;          // [n_streams][n_cb]
+    int32_t *codes;          // [n_streams][n_cb]; also carries each row's uniform between
+                             // the two kernels of a step
     int32_t *flags;          // [n_streams][n_cb] or nullptr
     int vec_logits;          // rows 16-byte aligned and vocab % 4 == 0
     int vec_hist;            // history rows 16-byte aligned and hist_len % 4 == 0
@@ -31,17 +34,22 @@ struct SampleArgs {
     // penalty reads the bitmap instead of scanning the ring, and the kernel
     // updates counts and bitmap for the token it evicts and the one it appends.
     uint16_t *counts;        // [n_streams][n_cb][vocab] or nullptr
-    uint32_t *presence;      // [n_streams][n_cb][allow_words] or nullptr
+    uint32_t *presence;      // [n_streams][n_cb][32] lane-major, or nullptr
 };
 
-// Enqueues one sampling step; returns the cudaError_t of the launch.
+// Enqueues one sampling step (the uniform draw, then the persistent sampler
+// under programmatic dependent launch); returns the cudaError_t of the launches.
 cudaError_t launch_sample(const SampleArgs &a, cudaStream_t stream);
 
-// Shared memory bytes the kernel uses for n_cb codebooks per CTA.
-size_t sample_smem_bytes(int n_cb);
+// Shared memory bytes of one sampler CTA.
+size_t sample_smem_bytes();
 
-// Rebuilds counts / presence of `rows` history rings ([rows][hist_len] i32,
-// entries outside [0, vocab) ignored).  hist_len <= 65535.
+// Reads and clears the sampler's device error word (1: a row copy did not
+// complete within ~2 s).  Returns a cudaError_t.
+int read_and_clear_sampler_error(int *value);
+
+// Rebuilds counts / lane-major presence of `rows` history rings
+// ([rows][hist_len] i32, entries outside [0, vocab) ignored).  hist_len <= 65535.
 cudaError_t launch_history_index(const int32_t *hist, long long rows, int hist_len, int vocab,
                                  uint16_t *counts, uint32_t *presence, cudaStream_t stream);
 
