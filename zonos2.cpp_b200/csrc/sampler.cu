@@ -531,38 +531,121 @@ __global__ void __launch_bounds__(128) draw_uniforms_kernel(uint64_t *rng, int n
 // Descending bitonic sort of 128 keys held four per lane (key e of lane l is
 // element 4*l + e): compare-exchanges inside a lane for distances 1 and 2,
 // shuffles across lanes for the rest.
-__device__ __forceinline__ void cmpx(uint64_t &a, uint64_t &b, bool desc)
+template <class Key>
+__device__ __forceinline__ void cmpx(Key &a, Key &b, bool desc)
 {
     const bool sw = desc ? (a < b) : (a > b);
-    const uint64_t x = sw ? b : a;
-    const uint64_t y = sw ? a : b;
+    const Key x = sw ? b : a;
+    const Key y = sw ? a : b;
     a = x;
     b = y;
 }
-__device__ __forceinline__ void bitonic128_desc(uint64_t key[4], int lane)
+template <class Key, int K, int J>
+__device__ __forceinline__ void bitonic_stage(Key key[4], int lane)
 {
-#pragma unroll 1
-    for (int k = 2; k <= 128; k <<= 1) {
-        const bool desc = ((4 * lane) & k) == 0;   // element 4l + e, k >= 4
-#pragma unroll 1
-        for (int j = k >> 1; j > 0; j >>= 1) {
-            if (j >= 4) {
-                const int lj = j >> 2;
-                const bool keep_max = desc == ((lane & lj) == 0);
+    const bool desc = ((4 * lane) & K) == 0;   // element 4l + e, K >= 4
+    if constexpr (J >= 4) {
+        constexpr int lj = J >> 2;
+        const bool keep_max = desc == ((lane & lj) == 0);
 #pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const uint64_t o = __shfl_xor_sync(kFull, key[e], lj);
-                    key[e] = ((key[e] > o) == keep_max) ? key[e] : o;
-                }
-            } else if (j == 2) {
-                cmpx(key[0], key[2], desc);
-                cmpx(key[1], key[3], desc);
-            } else {
-                cmpx(key[0], key[1], k == 2 ? true : desc);
-                cmpx(key[2], key[3], k == 2 ? false : desc);
-            }
+        for (int e = 0; e < 4; e++) {
+            const Key o = __shfl_xor_sync(kFull, key[e], lj);
+            key[e] = ((key[e] > o) == keep_max) ? key[e] : o;
         }
+    } else if constexpr (J == 2) {
+        cmpx(key[0], key[2], desc);
+        cmpx(key[1], key[3], desc);
+    } else if constexpr (K == 2) {
+        cmpx(key[0], key[1], true);
+        cmpx(key[2], key[3], false);
+    } else {
+        cmpx(key[0], key[1], desc);
+        cmpx(key[2], key[3], desc);
     }
+}
+template <class Key, int K>
+__device__ __forceinline__ void bitonic_merge(Key key[4], int lane)
+{
+    if constexpr (K >= 128) bitonic_stage<Key, K, 64>(key, lane);
+    if constexpr (K >= 64) bitonic_stage<Key, K, 32>(key, lane);
+    if constexpr (K >= 32) bitonic_stage<Key, K, 16>(key, lane);
+    if constexpr (K >= 16) bitonic_stage<Key, K, 8>(key, lane);
+    if constexpr (K >= 8) bitonic_stage<Key, K, 4>(key, lane);
+    if constexpr (K >= 4) bitonic_stage<Key, K, 2>(key, lane);
+    bitonic_stage<Key, K, 1>(key, lane);
+}
+// Out of line: the exact-key sort for the rare rows whose quantized order fails.
+__device__ __noinline__ void sort_keys_exact(uint64_t key[4], int lane);
+
+template <class Key>
+__device__ __forceinline__ void bitonic128_desc(Key key[4], int lane)
+{
+    bitonic_merge<Key, 2>(key, lane);
+    bitonic_merge<Key, 4>(key, lane);
+    bitonic_merge<Key, 8>(key, lane);
+    bitonic_merge<Key, 16>(key, lane);
+    bitonic_merge<Key, 32>(key, lane);
+    bitonic_merge<Key, 64>(key, lane);
+    bitonic_merge<Key, 128>(key, lane);
+}
+
+// Inclusive prefix sums, in f64, of the sorted probabilities at positions < m
+// (position 4*lane + e).  At most 128 f32 terms: each f64 add is exact or off by
+// 2^-53 relative, far inside the margins they are used with.
+__device__ __forceinline__ void prefix_f64(const uint64_t key[4], int m, int lane, double P[4])
+{
+    double run = 0.0;
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        run = __dadd_rn(run, (4 * lane + e < m) ? (double)key_p(key[e]) : 0.0);
+        P[e] = run;
+    }
+    double incl = run;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const double y = __shfl_up_sync(kFull, incl, o);
+        if (lane >= o) incl = __dadd_rn(incl, y);
+    }
+    double excl = __shfl_up_sync(kFull, incl, 1);
+    if (lane == 0) excl = 0.0;
+#pragma unroll
+    for (int e = 0; e < 4; e++) P[e] = __dadd_rn(P[e], excl);
+}
+
+__device__ __forceinline__ double sel4(const double P[4], int e)
+{
+    return e == 0 ? P[0] : e == 1 ? P[1] : e == 2 ? P[2] : P[3];
+}
+
+// P at position i, in every lane.
+__device__ __forceinline__ double prefix_at(const double P[4], int i)
+{
+    return __shfl_sync(kFull, sel4(P, i & 3), i >> 2);
+}
+
+// Smallest position 4*l + e whose bit e is set in lane l's f4; 128 if none.
+__device__ __forceinline__ int first_flagged(uint32_t f4)
+{
+    int best = 128;
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        const uint32_t b = __ballot_sync(kFull, (f4 >> e) & 1u);
+        if (b) best = min(best, 4 * (__ffs(b) - 1) + e);
+    }
+    return best;
+}
+
+// A partial sum the reference accumulates term by term in f32 over sorted
+// probabilities p_j (j <= i < 128), each divided by an f32 sum S' of at most 128
+// of them, is P_i / S * (1 + d) with P_i, S the exact sums and
+// |d| <= (i + 128 + 2) * 2^-24 (+ O(2^-48)): one rounding per division, per
+// add, and the sums' own rounding.  Decisions clear of the threshold by this
+// margin (taken 2.5x) equal the reference's; the rest are made term by term.
+constexpr double kSumEta = 640.0 * 0x1p-24;
+
+__device__ __noinline__ void sort_keys_exact(uint64_t key[4], int lane)
+{
+    bitonic128_desc(key, lane);
 }
 
 // Persistent: warp w of CTA b takes work items b + gridDim.x * w + k * W (W warps
@@ -597,16 +680,6 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
     const bool inc = a.presence != nullptr;
     const uint32_t row_bytes = 4u * (uint32_t)V;
     const uint32_t *slots = reinterpret_cast<const uint32_t *>(a.codes);
-    RowKnobs kn;
-    kn.V = V;
-    kn.K = K;
-    kn.topk_on = topk_on;
-    kn.top_p = a.top_p;
-    kn.min_p = a.min_p;
-    kn.rho = a.rho;
-    kn.inv_rho = a.inv_rho;
-    kn.inv_temp = a.inv_temp;
-    kn.pad = a.pad_id;
 
     // work items: (s, cb) of item it, advanced by the grid's warp count
     const long long step = (long long)gridDim.x * kWarps;
@@ -825,12 +898,23 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
             const float u = __uint_as_float(__ldcg(slots + r));
 
             if (!topk_on || n_c > kRegSortMax) {
+                RowKnobs kn;
+                kn.V = V;
+                kn.K = K;
+                kn.topk_on = topk_on;
+                kn.top_p = a.top_p;
+                kn.min_p = a.min_p;
+                kn.rho = a.rho;
+                kn.inv_rho = a.inv_rho;
+                kn.inv_temp = a.inv_temp;
+                kn.pad = a.pad_id;
                 tok = general_path(kn, region, lrow, selm, n_c, M, seenm, allowm, lane, u);
                 __syncwarp();
                 if (cb_nx < NCB) issue(s_nx, cb_nx);
             } else {
                 // ---- 5. candidates -> four per lane (compaction through shared memory)
                 uint64_t *stage = reinterpret_cast<uint64_t *>(region + kStageOffset);
+                float ymin = M;
                 {
                     const int cnt = __popc(selm);
                     int pos = warp_incl_scan(cnt, lane) - cnt;
@@ -839,38 +923,60 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
                         const int i = __ffs(sm) - 1;
                         sm &= sm - 1;
                         const int t = slot_token(lane, i);
-                        stage[pos++] = make_ent(rowf[t], t);
+                        const float y = rowf[t];
+                        ymin = fminf(ymin, y);
+                        stage[pos++] = make_ent(y, t);
                     }
                 }
+#pragma unroll
+                for (int o = 16; o; o >>= 1) ymin = fminf(ymin, __shfl_xor_sync(kFull, ymin, o));
                 __syncwarp();
-                uint64_t key[4];
+                // ---- 6. the (p desc, token asc) order.  p is a non-increasing function
+                // of the gap d = RN(max - l), so the candidates are sorted by a 32-bit
+                // key: d quantized to 22 bits over the candidates' range, then the
+                // token.  That is the exact order unless two gaps share a quantum or two
+                // gaps give one p; the order of the exact keys (p, token) is checked
+                // and, if broken, sorted outright.
+                uint32_t ck[4];
                 {
                     const ulonglong2 e01 = reinterpret_cast<const ulonglong2 *>(stage)[2 * lane];
                     const ulonglong2 e23 = reinterpret_cast<const ulonglong2 *>(stage)[2 * lane + 1];
-                    key[0] = e01.x;
-                    key[1] = e01.y;
-                    key[2] = e23.x;
-                    key[3] = e23.y;
+                    const uint64_t en[4] = {e01.x, e01.y, e23.x, e23.y};
+                    const float span = __fsub_rn(M, ymin);
+                    const float qs = span > 0.0f ? 4194000.0f / span : 0.0f;
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const float d = __fsub_rn(M, ent_v(en[e]));
+                        const uint32_t qd = min((uint32_t)__fmul_rn(d, qs), 4194302u);
+                        ck[e] = 4 * lane + e < n_c ? ~((qd << 10) | (uint32_t)en[e]) : 0u;
+                    }
                 }
-                __syncwarp();   // the row and the stage are free
-                if (cb_nx < NCB) issue(s_nx, cb_nx);
-
-                // ---- 6. exact probabilities (src/zonos2_generate.cpp:44-49) and the
-                // (p desc, token asc) order of the candidates
+                bitonic128_desc(ck, lane);
                 const SmemExpTable tab{exptab};
+                uint64_t key[4];
                 int np = 0;
 #pragma unroll
                 for (int e = 0; e < 4; e++) {
+                    key[e] = 0ull;   // sorts after every candidate
                     if (4 * lane + e < n_c) {
-                        const float p = row_prob(ent_v(key[e]), M, a.inv_temp, tab);
+                        const int t = (int)(~ck[e] & 1023u);
+                        const float p = row_prob(rowf[t], M, a.inv_temp, tab);
                         np += p > 0.0f;
-                        key[e] = make_key(p, (int)(uint32_t)key[e]);
-                    } else {
-                        key[e] = 0ull;   // sorts after every candidate
+                        key[e] = make_key(p, t);
                     }
                 }
                 const int n_pos = __reduce_add_sync(kFull, np);
-                bitonic128_desc(key, lane);
+                {
+                    const uint64_t nx = __shfl_down_sync(kFull, key[0], 1);
+                    const int i0 = 4 * lane;   // pairs (i, i + 1) with i + 1 < n_c
+                    const bool ok = (i0 + 1 >= n_c || key[0] > key[1]) &&
+                                    (i0 + 2 >= n_c || key[1] > key[2]) &&
+                                    (i0 + 3 >= n_c || key[2] > key[3]) &&
+                                    (i0 + 4 >= n_c || key[3] > nx);
+                    if (!__all_sync(kFull, ok)) sort_keys_exact(key, lane);
+                }
+                __syncwarp();   // the row and the stage are free
+                if (cb_nx < NCB) issue(s_nx, cb_nx);
                 uint64_t *keys = reinterpret_cast<uint64_t *>(region + kKeysOffset);
                 float *ps = reinterpret_cast<float *>(region + kPsOffset);
                 reinterpret_cast<ulonglong2 *>(keys)[2 * lane] = make_ulonglong2(key[0], key[1]);
@@ -883,18 +989,40 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
                 // list is keys[0..m) (positive probabilities, sorted) followed by
                 // zero-probability tokens in token order, n entries in all; every sum
                 // the reference recomputes from zero over a sorted prefix is one of
-                // the running prefix sums.
+                // the running prefix sums pf.  The top-p cut is found from exact
+                // prefix sums with the error margin above; only its own prefix is then
+                // summed term by term.
                 const int m = min(n_pos, K);
                 int n = K;
                 float *pf = reinterpret_cast<float *>(region + kPfOffset);
                 float *q = reinterpret_cast<float *>(region + kQOffset);
-                if (lane == 0) prefix_sums(ps, pf, m);
-                __syncwarp();
-                float S = pf[m - 1];
+                double P[4];
+                prefix_f64(key, m, lane, P);
+                int cut = -1;   // > 0: top-p certainly cuts after `cut` entries
                 if (a.top_p < 1.0f) {
-                    const int cut = walk_cdf(ps, q, m, S, a.top_p, lane);
-                    if (cut > 0) n = cut;  // never inside the zero tail: the sum stops growing
-                    S = pf[min(n, m) - 1];
+                    const double tpS = (double)a.top_p * prefix_at(P, m - 1);
+                    uint32_t nb = 0u;   // positions not certainly below top_p
+#pragma unroll
+                    for (int e = 0; e < 4; e++)
+                        if (4 * lane + e < m && !(P[e] * (1.0 + kSumEta) < tpS)) nb |= 1u << e;
+                    const int jj = first_flagged(nb);
+                    if (jj < 128 && prefix_at(P, jj) * (1.0 - kSumEta) >= tpS) cut = jj + 1;
+                }
+                float S;
+                if (cut > 0) {
+                    n = cut;
+                    if (lane == 0) prefix_sums(ps, pf, n);
+                    __syncwarp();
+                    S = pf[n - 1];
+                } else {   // no certain cut: the reference's sums and walk, term by term
+                    if (lane == 0) prefix_sums(ps, pf, m);
+                    __syncwarp();
+                    S = pf[m - 1];
+                    if (a.top_p < 1.0f) {
+                        const int c = walk_cdf(ps, q, m, S, a.top_p, lane);
+                        if (c > 0) n = c;  // never inside the zero tail: the sum stops growing
+                        S = pf[min(n, m) - 1];
+                    }
                 }
                 if (a.min_p > 0.0f) {
                     const float thresh = (ps[0] / S) * a.min_p;
@@ -904,8 +1032,24 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
                     n = j;
                     S = pf[min(n, m) - 1];
                 }
-                // ---- 8. one uniform, CDF walk (src/zonos2_generate.cpp:86-92)
-                const int hit = walk_cdf(ps, q, min(n, m), S, u, lane);
+                // ---- 8. one uniform, CDF walk (src/zonos2_generate.cpp:86-92): the
+                // first position whose partial sum reaches u, by the same margin
+                int hit;   // 1 + that position; -1 when the walk runs past the positives
+                {
+                    const int len = min(n, m);
+                    const double uS = (double)u * (double)S;
+                    uint32_t nb = 0u;   // positions not certainly below u
+#pragma unroll
+                    for (int e = 0; e < 4; e++)
+                        if (4 * lane + e < len && !(uS > P[e] * (1.0 + kSumEta))) nb |= 1u << e;
+                    const int jj = first_flagged(nb);
+                    if (jj == 128)
+                        hit = -1;
+                    else if (uS <= prefix_at(P, jj) * (1.0 - kSumEta))
+                        hit = jj + 1;
+                    else
+                        hit = walk_cdf(ps, q, len, S, u, lane);
+                }
                 if (lane == 0)
                     tok = pick_token(keys, hit > 0 ? hit - 1 : -1, n, m, n_pos,
                                      reinterpret_cast<uint32_t *>(region + kPosmapOffset), V,
