@@ -574,6 +574,64 @@ __device__ __forceinline__ void bitonic_merge(Key key[4], int lane)
     if constexpr (K >= 4) bitonic_stage<Key, K, 2>(key, lane);
     bitonic_stage<Key, K, 1>(key, lane);
 }
+// Bit i set for the slots of this lane that hold a token < V.
+__device__ __forceinline__ uint32_t valid_slots(int lane, int V)
+{
+    uint32_t m = 0u;
+#pragma unroll
+    for (int i = 0; i < 32; i++) m |= (slot_token(lane, i) < V ? 1u : 0u) << i;
+    return m;
+}
+
+// The row's slots -> registers when V < 1024 (slots past V read 0).
+__device__ __forceinline__ void load_row_partial(const float *rowf, int lane, int V, float v[32])
+{
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const int t0 = 4 * (lane + 32 * j);
+        float4 f = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (t0 < V) f = *reinterpret_cast<const float4 *>(rowf + t0);
+        v[4 * j + 0] = f.x;
+        v[4 * j + 1] = f.y;
+        v[4 * j + 2] = f.z;
+        v[4 * j + 3] = f.w;
+    }
+}
+
+// The prologue logit by logit, with the non-finite guard: for rows holding a
+// NaN or infinite logit, and for a penalty < 1.  Reloads the raw row, returns
+// this lane's max; drops non-finite slots from *km, flags them in *nonfin.
+__device__ __forceinline__ float careful_prologue(const float *rowf, int lane, int V, uint32_t seenm,
+                                               uint32_t allowm, uint32_t validm, float rho,
+                                               float inv_rho, float v[32], uint32_t *km,
+                                               bool *nonfin)
+{
+    float mx = -INFINITY;
+    uint32_t finm = 0u;
+    bool nf = false;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const int t0 = 4 * (lane + 32 * j);
+        float4 f = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (t0 < V) f = *reinterpret_cast<const float4 *>(rowf + t0);
+        v[4 * j + 0] = f.x;
+        v[4 * j + 1] = f.y;
+        v[4 * j + 2] = f.z;
+        v[4 * j + 3] = f.w;
+    }
+#pragma unroll
+    for (int i = 0; i < 32; i++) {
+        const bool fin = v[i] < INFINITY;
+        nf |= !fin;
+        finm |= (fin ? 1u : 0u) << i;
+        v[i] = prologue(v[i], i, seenm, allowm & validm, rho, inv_rho);
+        mx = fmaxf(mx, v[i]);
+    }
+    *km &= finm;
+    *nonfin = nf;
+    return mx;
+}
+
 // Out of line: the exact-key sort for the rare rows whose quantized order fails.
 __device__ __noinline__ void sort_keys_exact(uint64_t key[4], int lane);
 
@@ -787,26 +845,47 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
             __syncwarp();
         }
         pending = false;
+        // slots at or past the vocabulary never enter a row
+        const uint32_t validm = V >= 1024 ? ~0u : valid_slots(lane, V);
         float v[32];
+        if (V >= 1024) {
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const int t0 = 4 * (lane + 32 * j);
-            float4 f = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-            if (t0 < V) f = *reinterpret_cast<const float4 *>(rowf + t0);
-            v[4 * j + 0] = f.x;
-            v[4 * j + 1] = f.y;
-            v[4 * j + 2] = f.z;
-            v[4 * j + 3] = f.w;
+            for (int j = 0; j < 8; j++) {
+                const float4 f = *reinterpret_cast<const float4 *>(rowf + 4 * (lane + 32 * j));
+                v[4 * j + 0] = f.x;
+                v[4 * j + 1] = f.y;
+                v[4 * j + 2] = f.z;
+                v[4 * j + 3] = f.w;
+            }
+        } else {
+            load_row_partial(rowf, lane, V, v);
         }
 
-        // ---- 3. prologue and row max; the row is rewritten in place
-        bool nonfin = false;
+        // ---- 3. prologue and row max; the row is rewritten in place.  Fast form
+        // for a penalty >= 1 and finite logits: the penalized logit is
+        // min(l * RN(1/rho), l * rho), which is the reference's pick of the two,
+        // and one fma per logit (l * 0 + acc) leaves acc nonzero if any logit is
+        // NaN or infinite; such rows (and a penalty < 1) take the careful form.
         float mx = -INFINITY;
+        uint32_t km = allowm & validm;   // slots that keep their logit
+        bool nonfin = false;
+        {
+            float acc = 1.0f;
+            if (a.rho >= 1.0f) {
+                acc = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 32; i++) {
-            nonfin |= !(v[i] < INFINITY);
-            v[i] = prologue(v[i], i, seenm, allowm, a.rho, a.inv_rho);
-            mx = fmaxf(mx, v[i]);
+                for (int i = 0; i < 32; i++) {
+                    const float x = v[i];
+                    acc = __fmaf_rn(x, 0.0f, acc);
+                    const float pn = fminf(__fmul_rn(x, a.inv_rho), __fmul_rn(x, a.rho));
+                    const float z = ((seenm >> i) & 1u) ? pn : x;
+                    v[i] = ((km >> i) & 1u) ? z : -INFINITY;
+                    mx = fmaxf(mx, v[i]);
+                }
+            }
+            if (__any_sync(kFull, !(acc == 0.0f)))
+                mx = careful_prologue(rowf, lane, V, seenm, allowm, validm, a.rho, a.inv_rho, v,
+                                      &km, &nonfin);
         }
 #pragma unroll
         for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
@@ -822,31 +901,31 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
             const float M = mx;
             const float T = a.temperature;
             // ---- 4. gap histogram and the bucket of the k-th largest logit.  The
-            // open-ended last bucket holds most of a row: it is not counted with
-            // atomics, its count follows from the number of finite logits.
+            // open-ended last bucket holds most of a row: it is not counted, its
+            // count follows from the number of kept logits.
             const float bw = fmaxf(T * 0.125f, fabsf(M) * 0x1p-18f + T * 0x1p-14f);
             const float sc = 1.0f / bw;
             const float Msc = M * sc;
             reinterpret_cast<uint4 *>(hist)[lane] = make_uint4(0u, 0u, 0u, 0u);
             __syncwarp();
-            int nf = 0;
+            // bucket_bits = 0x4B000000 + b, so (bits * 4 + hbase) mod 2^32 is the
+            // shared address of counter b
+            const uint32_t hbase = smem_u32(hist) - 0x2C000000u;
 #pragma unroll
             for (int j = 0; j < 8; j++) {
                 uint32_t bb[4];
 #pragma unroll
                 for (int e = 0; e < 4; e++) {
-                    const float x = v[4 * j + e];
-                    const bool fin = x > -INFINITY;
-                    const uint32_t bits = bucket_bits(x, sc, Msc);
-                    const uint32_t b = bits & 0x7fu;
-                    if (b < (uint32_t)(kBuckets - 2)) atomicAdd(hist + b, 1u);  // -inf: 126
-                    nf += fin;
-                    bb[e] = fin ? bits : (uint32_t)(kBuckets - 1);
+                    const uint32_t bits = bucket_bits(v[4 * j + e], sc, Msc);
+                    if (bits < 0x4B000000u + (uint32_t)(kBuckets - 2))
+                        asm volatile("red.shared.add.u32 [%0], 1;" ::"r"(bits * 4u + hbase)
+                                     : "memory");
+                    bb[e] = bits;
                 }
                 bkt[lane + 32 * j] = __byte_perm(__byte_perm(bb[0], bb[1], 0x0040u),
                                                  __byte_perm(bb[2], bb[3], 0x0040u), 0x5410u);
             }
-            const int n_fin = __reduce_add_sync(kFull, nf);
+            const int n_fin = __reduce_add_sync(kFull, __popc(km));
             __syncwarp();
             const uint4 h4 = reinterpret_cast<const uint4 *>(hist)[lane];
             int h[4] = {(int)h4.x, (int)h4.y, (int)h4.z, (int)h4.w};
@@ -889,6 +968,7 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
             uint32_t selm = 0u;   // this lane's candidate slots
 #pragma unroll
             for (int j = 0; j < 8; j++) selm |= bytes_le(bkt[lane + 32 * j], bc4) << (4 * j);
+            selm &= km;
 
             // the uniform: its producer has finished once waited for
             if (!drawn) {
@@ -915,17 +995,21 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
                 // ---- 5. candidates -> four per lane (compaction through shared memory)
                 uint64_t *stage = reinterpret_cast<uint64_t *>(region + kStageOffset);
                 float ymin = M;
-                {
+                {   // as many rounds as the fullest lane needs, without branches: a lane
+                    // with nothing left writes a spare entry past the stage
                     const int cnt = __popc(selm);
                     int pos = warp_incl_scan(cnt, lane) - cnt;
+                    const int rounds = __reduce_max_sync(kFull, (unsigned)cnt);
                     uint32_t sm = selm;
-                    while (sm) {
-                        const int i = __ffs(sm) - 1;
-                        sm &= sm - 1;
+                    for (int k = 0; k < rounds; k++) {
+                        const bool has = sm != 0u;
+                        const int i = __ffs(sm | 0x80000000u) - 1;
+                        sm &= sm - 1u;
                         const int t = slot_token(lane, i);
                         const float y = rowf[t];
-                        ymin = fminf(ymin, y);
-                        stage[pos++] = make_ent(y, t);
+                        ymin = has ? fminf(ymin, y) : ymin;
+                        stage[has ? pos : kRegSortMax] = make_ent(y, t);
+                        pos += has;
                     }
                 }
 #pragma unroll
