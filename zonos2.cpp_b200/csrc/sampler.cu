@@ -168,6 +168,15 @@ __device__ __forceinline__ uint32_t bucket_bits(float v, float sc, float Msc)
     return __float_as_uint(__fadd_rn(t, 0x1p23f));
 }
 
+// The bucket coordinate of bucket_bits, (max - v) / width + 1/2 in [0, 126.5],
+// rounded to a multiple of 2^-15: an integer below 2^22, monotone
+// non-increasing in v.
+__device__ __forceinline__ uint32_t gap_q15(float v, float sc, float Msc)
+{
+    const float t = fminf(__fmaf_rn(-v, sc, Msc), (float)(kBuckets - 2));
+    return __float_as_uint(__fmaf_rn(t, 32768.0f, 16384.0f + 0x1p23f)) - 0x4B000000u;
+}
+
 // Bit e of the result is set iff byte e of pk is <= bc (bytes and bc < 128).
 __device__ __forceinline__ uint32_t bytes_le(uint32_t pk, uint32_t bc4)
 {
@@ -992,9 +1001,15 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
                 __syncwarp();
                 if (cb_nx < NCB) issue(s_nx, cb_nx);
             } else {
-                // ---- 5. candidates -> four per lane (compaction through shared memory)
-                uint64_t *stage = reinterpret_cast<uint64_t *>(region + kStageOffset);
-                float ymin = M;
+                // ---- 5. candidates -> four per lane, as 32-bit sort keys (compaction
+                // through shared memory).  p is a non-increasing function of the gap,
+                // so the keys order the candidates by the gap's bucket coordinate
+                // (max - l) / width, monotone in l like the bucket and kept to 15
+                // fractional bits, then by token.  That is the exact (p desc, token asc)
+                // order unless two gaps share a quantum or two gaps give one p; the
+                // order of the exact keys is checked below and, if broken, sorted
+                // outright.
+                uint32_t *stage = reinterpret_cast<uint32_t *>(region + kStageOffset);
                 {   // as many rounds as the fullest lane needs, without branches: a lane
                     // with nothing left writes a spare entry past the stage
                     const int cnt = __popc(selm);
@@ -1006,34 +1021,19 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
                         const int i = __ffs(sm | 0x80000000u) - 1;
                         sm &= sm - 1u;
                         const int t = slot_token(lane, i);
-                        const float y = rowf[t];
-                        ymin = has ? fminf(ymin, y) : ymin;
-                        stage[has ? pos : kRegSortMax] = make_ent(y, t);
+                        stage[has ? pos : kRegSortMax] =
+                            ~((gap_q15(rowf[t], sc, Msc) << 10) | (uint32_t)t);
                         pos += has;
                     }
                 }
-#pragma unroll
-                for (int o = 16; o; o >>= 1) ymin = fminf(ymin, __shfl_xor_sync(kFull, ymin, o));
                 __syncwarp();
-                // ---- 6. the (p desc, token asc) order.  p is a non-increasing function
-                // of the gap d = RN(max - l), so the candidates are sorted by a 32-bit
-                // key: d quantized to 22 bits over the candidates' range, then the
-                // token.  That is the exact order unless two gaps share a quantum or two
-                // gaps give one p; the order of the exact keys (p, token) is checked
-                // and, if broken, sorted outright.
                 uint32_t ck[4];
                 {
-                    const ulonglong2 e01 = reinterpret_cast<const ulonglong2 *>(stage)[2 * lane];
-                    const ulonglong2 e23 = reinterpret_cast<const ulonglong2 *>(stage)[2 * lane + 1];
-                    const uint64_t en[4] = {e01.x, e01.y, e23.x, e23.y};
-                    const float span = __fsub_rn(M, ymin);
-                    const float qs = span > 0.0f ? 4194000.0f / span : 0.0f;
-#pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        const float d = __fsub_rn(M, ent_v(en[e]));
-                        const uint32_t qd = min((uint32_t)__fmul_rn(d, qs), 4194302u);
-                        ck[e] = 4 * lane + e < n_c ? ~((qd << 10) | (uint32_t)en[e]) : 0u;
-                    }
+                    const uint4 k4 = reinterpret_cast<const uint4 *>(stage)[lane];
+                    ck[0] = 4 * lane + 0 < n_c ? k4.x : 0u;
+                    ck[1] = 4 * lane + 1 < n_c ? k4.y : 0u;
+                    ck[2] = 4 * lane + 2 < n_c ? k4.z : 0u;
+                    ck[3] = 4 * lane + 3 < n_c ? k4.w : 0u;
                 }
                 bitonic128_desc(ck, lane);
                 const SmemExpTable tab{exptab};
