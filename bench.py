@@ -58,10 +58,13 @@ ROW_BYTES = 4 * VOCAB + 4 * HIST + 8 + 128 / NCB
 # presence bitmap of the history instead of the ring, ring read + write,
 # two u16 counts read and written, code and flag, allow bits, generator state.
 DESIGN_ROW_BYTES = 4 * VOCAB + 128 + 8 + 8 + 8 + 128 / NCB + 64 / NCB
-# DRAM bytes (read + write) of one sample_kernel<288,3> launch on this
-# workload, from an ncu capture of `bench.py --steps 3 --warmup 3`
-# (dram__bytes_read.sum 170.35 MB + dram__bytes_write.sum 9.60 MB).
-SAMPLER_TRAFFIC_BYTES = 179.94e6
+# DRAM bytes (read + write) of one sample_rows_kernel launch on this workload,
+# from an ncu capture of `bench.py --steps 12 --warmup 3 --no-cpu-baseline
+# --no-head`, launch 11 (dram__bytes_read.sum 170.45 MB +
+# dram__bytes_write.sum 6.11 MB).
+SAMPLER_TRAFFIC_BYTES = 176.56e6
+# Kernels of ours per decode step: the uniform draw and the persistent sampler.
+LAUNCHES_PER_STEP = 2
 
 
 def dist_env():
@@ -436,14 +439,15 @@ def run_ours(args):
                    "l2": "inputs larger than L2 (151 MB logits + 151 MB history per GPU per step)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": args.traffic,
-                     "kernel": "sample_kernel<288,3>", "kernel_ms": kern_ms,
+                     "kernel": "sample_rows_kernel (+ draw_uniforms_kernel)",
+                     "kernel_ms": kern_ms,
                      "bytes_per_launch": launch_bytes, "peak_source": peak_src,
                      "design_bytes_per_launch": DESIGN_ROW_BYTES * rows,
                      "design_frac": DESIGN_ROW_BYTES * rows / (kern_ms / 1e3) / 1e9 / peak},
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": "codes/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps},
-        "gpu_launches": args.steps,
+        "gpu_launches": LAUNCHES_PER_STEP * args.steps,
         "head": head,
         "clocks": clocks.result() if clocks else None,
     }
