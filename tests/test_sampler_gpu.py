@@ -312,3 +312,58 @@ def test_context_incremental_history_rollout(z2, oracle, cuda, H):
     torch.cuda.synchronize()
     assert (codes.cpu().numpy() == oc).all()
     ctx.close()
+
+
+def _state_with_first_uniform(oracle, u, seed):
+    """A generator state whose first draw gives the f32 uniform `u` (a multiple
+    of 2^-24): the output rotl(s1 * 5, 7) * 9 is inverted for s1 (5 and 9 are
+    odd, so invertible mod 2^64); s0, s2, s3 come from a seeded state."""
+    M64 = (1 << 64) - 1
+    out = (int(round(u * 2 ** 53)) << 11) & M64
+    x = (out * pow(9, -1, 1 << 64)) & M64
+    x = ((x >> 7) | (x << 57)) & M64          # rotr 7
+    s1 = (x * pow(5, -1, 1 << 64)) & M64
+    st = oracle.rng_seed(seed).copy()
+    st[1] = np.uint64(s1)
+    assert oracle.randf(st.copy()) == np.float32(u)
+    return st
+
+
+def test_sampler_exact_fallbacks(z2, oracle, cuda):
+    """Rows built to leave the fast paths: (a) a penalty < 1 (the prologue logit
+    by logit), (b) pairs of logits one ulp apart with their tokens in reverse
+    order (the quantized sort keys tie, the exact order check re-sorts), (c) a
+    uniform exactly on a partial sum of the CDF (the walk term by term)."""
+    rs = np.random.default_rng(21)
+    S, Cb, V, H = 8, 9, 1024, 64
+    lg = softcapped(rs, (S, Cb, V), 3.0)
+    # (b) streams 0-3: 24 one-ulp pairs near each row's top, larger logit on the larger token
+    for s in range(4):
+        for c in range(Cb):
+            row = lg[s, c]
+            top = float(row.max())
+            toks = rs.choice(V, size=48, replace=False)
+            for a_, b_ in zip(sorted(toks[:24]), sorted(toks[24:])):
+                lo_t, hi_t = min(a_, b_), max(a_, b_)
+                v = np.float32(top - rs.uniform(0.05, 1.5))
+                row[hi_t] = v
+                row[lo_t] = np.nextafter(v, np.float32(-np.inf))
+    # (c) streams 4-7, codebook 0: four equal maxima, top-k 4 -> CDF 1/4, 1/2, 3/4, 1;
+    # the stream's first uniform is exactly 1/2
+    for s in range(4, 8):
+        lg[s, 0, :] = -20.0
+        lg[s, 0, [3, 100, 517, 1000]] = 5.0
+    hist = rs.integers(0, V, (S, Cb, H), dtype=np.int32)
+    for s in range(4, 8):   # keep the four maxima unpenalised, hence equal
+        h0 = hist[s, 0]
+        h0[np.isin(h0, [3, 100, 517, 1000])] = 0
+    rng = oracle.rng_seed_streams(11, S)
+    for s in range(4, 8):
+        rng[s] = _state_with_first_uniform(oracle, 0.5, 100 + s)
+    for rho in (1.15, 0.85):   # (a): 0.85 < 1
+        prm = make_params(0.7, 4, 0.9, 0.0, rho, 1023)
+        g, o = run_step(z2, oracle, cuda, lg, prm, rng.copy(), hist.copy(), hist_pos=5)
+        assert_exact(g, o, f"top-k 4, penalty {rho}")
+        prm = make_params(0.7, 100, 0.9, 0.02, rho, 1023)
+        g, o = run_step(z2, oracle, cuda, lg, prm, rng.copy(), hist.copy(), hist_pos=5)
+        assert_exact(g, o, f"top-k 100, penalty {rho}")
