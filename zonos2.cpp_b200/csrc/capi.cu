@@ -254,7 +254,7 @@ struct zonos2cu_ctx {
     uint64_t *rng = nullptr;     // [S][4]
     int32_t *hist = nullptr;     // [S][C][H]
     int hist_pos = 0;
-    uint16_t *counts = nullptr;  // [S][C][V] occurrences of each token in the ring
+    uint16_t *counts = nullptr;  // [S][C][1024] occurrences of each token in the ring
     uint32_t *presence = nullptr;// [S][C][32] tokens with a nonzero count, lane-major
     uint32_t *allow = nullptr;   // [S][32] lane-major (word l, bit 4j+e: token 4(l+32j)+e)
     bool allow_on = false;
@@ -343,7 +343,8 @@ int zonos2cu_ctx_create(int device, const zonos2cu_dims *d, zonos2cu_ctx **out)
         if (d->hist_len > 0) {
             const size_t rows = S * d->n_cb;
             const size_t hb = sizeof(int32_t) * rows * (size_t)d->hist_len;
-            const size_t cbytes = sizeof(uint16_t) * rows * (size_t)d->vocab;
+            // u16 counts, rows 1024 wide (word-aligned pairs for the sampler's atomics)
+            const size_t cbytes = sizeof(uint16_t) * rows * (size_t)z2::kSamplerVocabMax;
             const size_t pbytes = sizeof(uint32_t) * rows * 32;   // lane-major 1024-bit map
             e = cudaMalloc(&c->hist, hb);
             if (e == cudaSuccess) e = cudaMemsetAsync(c->hist, 0xff, hb, c->stream);  // -1: empty

@@ -760,6 +760,7 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
     bool drawn = false;     // the draw grid has been waited for
     bool pending = false;   // the copy of the current row is in flight
     uint32_t seen_next = 0u, allow_next = ~0u;   // lane-major masks of the next row
+    int ev_next = -1;   // lane 0: the token the next row's append evicts
 
     // Starts the bulk copy of row (s2, cb2) and loads its lane-major masks.
     auto issue = [&](int s2, int cb2) {
@@ -771,6 +772,7 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
         }
         if (pen && inc) seen_next = __ldcg(a.presence + (size_t)r2 * 32 + lane);
         if (a.allow && a.allow_lane_major) allow_next = __ldg(a.allow + (size_t)s2 * 32 + lane);
+        if (inc && lane == 0) ev_next = __ldcg(a.hist + (size_t)r2 * a.hist_len + a.hist_pos);
         pending = true;
     };
     if (cb < NCB) issue(s, cb);
@@ -787,6 +789,7 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
 
         // ---- 1. the history's token set and the allow bits
         uint32_t seenm = seen_next, allowm = ~0u;
+        const int ev = ev_next;
         if (pen && !inc) {   // scan the ring into seen-bytes
             unsigned char *seen = region + kBktOffset;
             uint4 *seen4 = reinterpret_cast<uint4 *>(seen);
@@ -900,6 +903,14 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
         for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
         const bool live = mx >= -1e9f;  // running max starts at -1e9: :41-42
         const int flag = (__any_sync(kFull, nonfin) ? 2 : 0) | (live ? 0 : 1);
+        // The evicted token leaves the history index now that the row's set has been
+        // read: its count drops (two u16 counts per word); the old count comes back
+        // by the end of the row.
+        uint32_t ev_old = 0u;
+        if (inc && lane == 0 && (unsigned)ev < (unsigned)V)
+            ev_old = atomicSub(reinterpret_cast<uint32_t *>(a.counts + (size_t)r * kSamplerVocabMax) +
+                                   (ev >> 1),
+                               1u << (16 * (ev & 1)));
 
         int tok = a.pad_id;
         if (live && !forced) {
@@ -1154,19 +1165,15 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
             if (a.flags) a.flags[r] = flag;
             if (a.hist && a.hist_len > 0) {
                 int32_t *ring = a.hist + (size_t)r * a.hist_len;
-                if (inc) {   // the evicted token leaves the index, the new one enters
-                    const int ev = __ldcg(ring + a.hist_pos);
-                    uint16_t *cnt = a.counts + (size_t)r * V;
+                if (inc) {   // no waits: reductions, in this order on shared words
                     uint32_t *pm = a.presence + (size_t)r * 32;
-                    if ((unsigned)ev < (unsigned)V) {
-                        const unsigned c = cnt[ev] - 1u;
-                        cnt[ev] = (uint16_t)c;
-                        if (c == 0u) pm[lm_word(ev)] &= ~lm_bit(ev);
-                    }
+                    uint32_t *cnt32 =
+                        reinterpret_cast<uint32_t *>(a.counts + (size_t)r * kSamplerVocabMax);
+                    if ((unsigned)ev < (unsigned)V && ((ev_old >> (16 * (ev & 1))) & 0xffffu) == 1u)
+                        atomicAnd(pm + lm_word(ev), ~lm_bit(ev));   // its last occurrence left
                     if ((unsigned)tok < (unsigned)V) {
-                        const unsigned c = cnt[tok];
-                        cnt[tok] = (uint16_t)(c + 1u);
-                        if (c == 0u) pm[lm_word(tok)] |= lm_bit(tok);
+                        atomicAdd(cnt32 + (tok >> 1), 1u << (16 * (tok & 1)));
+                        atomicOr(pm + lm_word(tok), lm_bit(tok));
                     }
                 }
                 ring[a.hist_pos] = tok;
@@ -1198,7 +1205,8 @@ __global__ void __launch_bounds__(256) history_index_kernel(const int32_t *hist,
         if ((unsigned)t < (unsigned)V) atomicAdd(cw + t, 1u);
     }
     __syncwarp();
-    for (int t = lane; t < V; t += 32) counts[row * (size_t)V + t] = (uint16_t)cw[t];
+    for (int t = lane; t < kSamplerVocabMax; t += 32)
+        counts[row * (size_t)kSamplerVocabMax + t] = (uint16_t)cw[t];
     uint32_t bits = 0u;
 #pragma unroll
     for (int i = 0; i < 32; i++) bits |= (cw[slot_token(lane, i)] > 0u ? 1u : 0u) << i;

@@ -33,7 +33,7 @@ struct SampleArgs {
     // occurs in the ring and a bitmap of the tokens that occur.  When set, the
     // penalty reads the bitmap instead of scanning the ring, and the kernel
     // updates counts and bitmap for the token it evicts and the one it appends.
-    uint16_t *counts;        // [n_streams][n_cb][vocab] or nullptr
+    uint16_t *counts;        // [n_streams][n_cb][1024] or nullptr
     uint32_t *presence;      // [n_streams][n_cb][32] lane-major, or nullptr
 };
 
