@@ -67,21 +67,25 @@ def test_head_bf16_tcgen05(z2, oracle, cuda, B, rpc):
     assert err.max() <= 1e-3
 
 
-def test_head_bf16_large_batch_rows(z2, oracle, cuda):
-    """A 4096-row launch (persistent tiles, both accumulators): rows spot-checked."""
+@pytest.mark.parametrize("B,rpc", [(4096, 1024), (1000, 1026), (1100, 1024)])
+def test_head_bf16_large_batch_rows(z2, oracle, cuda, B, rpc):
+    """Batches large enough for the two-SM kernel (256 x 256 tiles over CTA
+    pairs, both accumulators; 1000 and 1100 leave the last tile ragged, 1100
+    with an odd count of 128-row blocks): rows spot-checked against the oracle,
+    every row against a torch f32 matmul of the same bf16 values."""
     import torch
-    rs = np.random.default_rng(11)
-    B = 4096
-    Wb, Wf = _bf16(rs.normal(0, 0.02, size=(9 * 1024, 2048)).astype(np.float32))
+    rs = np.random.default_rng(11 + B)
+    Wb, Wf = _bf16(rs.normal(0, 0.02, size=(9 * rpc, 2048)).astype(np.float32))
     hb, hf = _bf16(rs.normal(0, 1, size=(B, 2048)).astype(np.float32))
-    out = torch.empty((B, 9, 1024), dtype=torch.float32, device=cuda)
-    z2.head_softcap(_dev(Wb, cuda), z2.BF16, 1024, 9, 1024, _dev(hb, cuda), out)
+    out = torch.full((B, 9, 1024), float("nan"), dtype=torch.float32, device=cuda)
+    z2.head_softcap(_dev(Wb, cuda), z2.BF16, rpc, 9, 1024, _dev(hb, cuda), out)
     torch.cuda.synchronize()
     assert z2.device_error() == 0
-    rows = np.array([0, 1, 127, 128, 2047, 2048, 3333, 4095])
-    ref = oracle.head_softcap(Wf, 1024, 9, 1024, hf[rows])
+    rows = np.unique(np.array([0, 1, 127, 128, 255, 256, B // 2, B - 129, B - 1]))
+    ref = oracle.head_softcap(Wf, rpc, 9, 1024, hf[rows])
     got = out.cpu().numpy()[rows]
     assert np.abs(got - ref).max() <= 1e-3
-    # every row against a torch f32 matmul of the same bf16 values
-    full = torch.tanh(torch.from_numpy(hf).to(cuda) @ torch.from_numpy(Wf).to(cuda).T / 15) * 15
+    Wk = torch.from_numpy(Wf.reshape(9, rpc, 2048)[:, :1024].reshape(9 * 1024, 2048)).to(cuda)
+    full = torch.tanh(torch.from_numpy(hf).to(cuda) @ Wk.T / 15) * 15
+    assert torch.isfinite(out).all().item()
     assert (out.reshape(B, -1) - full).abs().max().item() <= 1e-3

@@ -342,6 +342,297 @@ __global__ void __launch_bounds__(kThreads, 1)
                      : "memory");
 }
 
+// ---- two-SM pairs (cluster of 2, tcgen05 cta_group::2) ----------------------
+__device__ __forceinline__ uint32_t cluster_rank()
+{
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// Address of this CTA's shared variable `addr` in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t peer_addr(uint32_t addr, uint32_t rank)
+{
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+// mbar_wait with cluster-scope acquire: for barriers that the other CTA of the
+// pair arrives on.
+__device__ __forceinline__ bool mbar_try_wait_cl(uint32_t bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cl(uint32_t bar, uint32_t parity)
+{
+    if (mbar_try_wait_cl(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 1;; it++) {
+        if (mbar_try_wait_cl(bar, parity)) return true;
+        if ((it & 255u) == 0u && globaltimer_ns() - t0 > kWaitNs) {
+            atomicCAS(&g_device_error, 0, kErrTimeout);
+            return false;
+        }
+    }
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr)
+{
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+                 : "memory");
+}
+__device__ __forceinline__ void cluster_sync()
+{
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                     : "memory");
+}
+__device__ __forceinline__ void mma_bf16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                              uint32_t idesc, uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrives on the mbarrier at cluster address `bar` once the pair's MMAs issued
+// so far have completed.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar)
+{
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     bar)
+                 : "memory");
+}
+
+// Persistent two-SM version for large batches: the two CTAs of a cluster
+// compute a 256 x 256 tile with tcgen05.mma.cta_group::2 (M=256, N=256,
+// K=16), each holding half of the A rows and half of the B rows in its own
+// shared memory and half of the accumulator rows in its own TMEM.  Per SM and
+// 64-deep K step that is 32 KB of operands instead of 48 KB for the same MMA
+// work, which is what limits the one-SM kernel (its operands come from L2).
+//   warp 0 (both CTAs)   TMA producer of the CTA's halves, on its own `full`;
+//   warp 1, rank 0       issues the pair's MMAs once both halves are in: its
+//                        own `full`, and `pfull`, where warp 1 of rank 1
+//                        forwards the completion of rank 1's `full`;
+//                        commits release `empty` and signal `tfull` in both CTAs;
+//   warps 2..5 (both)    epilogue of the CTA's 128 accumulator rows, then an
+//                        arrive on rank 0's `tempty` (256 arrivals).
+// No load is multicast: every copy lands in the CTA that issued it.
+template <int STAGES>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    head_tc2_kernel(const __grid_constant__ CUtensorMap map_a,
+                    const __grid_constant__ CUtensorMap map_b, const TcArgs args)
+{
+    constexpr int BN = 256;                    // N of the pair's tile; each CTA holds 128 B rows
+    constexpr uint32_t kABytes = kBM * kBK * 2;
+    constexpr uint32_t kBBytes = (BN / 2) * kBK * 2;
+    constexpr uint32_t kStageBytes = kABytes + kBBytes;
+    constexpr uint32_t kTmemCols = 2 * BN;
+    constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                ((uint32_t)((2 * kBM) >> 4) << 24);
+
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *smem = reinterpret_cast<unsigned char *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * kStageBytes);
+    // bars: full[STAGES], empty[STAGES], tfull[2], tempty[2], pfull[STAGES]; the TMEM slot
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * STAGES + 4);
+    __shared__ int s_abort;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const int KB = args.dim / kBK;
+    auto full = [&](int s) { return smem_u32(bars + s); };
+    auto empty = [&](int s) { return smem_u32(bars + STAGES + s); };
+    auto tfull = [&](int a) { return smem_u32(bars + 2 * STAGES + a); };
+    auto tempty = [&](int a) { return smem_u32(bars + 2 * STAGES + 2 + a); };
+    auto pfull = [&](int s) { return smem_u32(bars + 2 * STAGES + 4 + s); };
+
+    if (threadIdx.x == 0) {
+        s_abort = 0;
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(full(s), 1);
+            mbar_init(empty(s), 1);
+            mbar_init(pfull(s), 1);
+        }
+        for (int a = 0; a < 2; a++) {
+            mbar_init(tfull(a), 1);
+            mbar_init(tempty(a), 256);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        prefetch_map(&map_a);
+        prefetch_map(&map_b);
+    }
+    if (warp == 1) {   // both CTAs, same warp: one allocation across the pair
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();    // barriers of both CTAs initialised before any remote arrive
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
+    const int tiles_m2 = (args.tiles_m + 1) >> 1;   // 256-row blocks
+    const int per_cb = args.vocab / BN;
+    const int n_tiles = tiles_m2 * args.n_cb * per_cb;
+
+    if (warp == 0) {
+        // ---- TMA producer (this CTA's halves)
+        if (lane == 0) {
+            int it = 0;
+            bool ok = true;
+            for (int tile = pair; tile < n_tiles && ok; tile += n_pairs) {
+                const int mt = tile % tiles_m2, nt = tile / tiles_m2;
+                const int c = nt / per_cb, t = nt % per_cb;
+                const int a_row = mt * 2 * kBM + (int)rank * kBM;
+                const int b_row = c * args.rows_per_cb + t * BN + (int)rank * (BN / 2);
+                for (int kb = 0; kb < KB; kb++, it++) {
+                    const int s = it % STAGES;
+                    const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+                    if (!mbar_wait(empty(s), ph ^ 1u) || *(volatile int *)&s_abort) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t sa = smem_u32(smem + s * kStageBytes);
+                    mbar_expect_tx(full(s), kStageBytes);
+                    tma_load_2d(sa, &map_a, kb * kBK, a_row, full(s));
+                    tma_load_2d(sa + kABytes, &map_b, kb * kBK, b_row, full(s));
+                }
+            }
+            if (!ok) {
+                s_abort = 1;
+                // this CTA's copies still in flight land before it leaves
+                for (int k = 0; k < STAGES && k < it; k++) {
+                    const int j = it - 1 - k;
+                    mbar_wait(full(j % STAGES), (uint32_t)(j / STAGES) & 1u);
+                }
+            }
+        }
+    } else if (warp == 1 && rank == 1) {
+        // ---- forwards "stage s of rank 1 is in" to rank 0's pfull(s)
+        if (lane == 0) {
+            int it = 0;
+            for (int tile = pair; tile < n_tiles; tile += n_pairs) {
+                bool ok = true;
+                for (int kb = 0; kb < KB; kb++, it++) {
+                    const int s = it % STAGES;
+                    const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+                    if (!mbar_wait(full(s), ph) || *(volatile int *)&s_abort) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_cluster(peer_addr(pfull(s), 0));
+                }
+                if (!ok) {
+                    s_abort = 1;
+                    break;
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---- MMA issuer (rank 0) for the pair
+        if (lane == 0) {
+            int it = 0, local = 0;
+            bool ok = true;
+            for (int tile = pair; tile < n_tiles && ok; tile += n_pairs, local++) {
+                const int acc = local & 1;
+                const uint32_t aph = (uint32_t)(local >> 1) & 1u;
+                if (!mbar_wait_cl(tempty(acc), aph ^ 1u)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+                for (int kb = 0; kb < KB; kb++, it++) {
+                    const int s = it % STAGES;
+                    const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+                    if (!mbar_wait(full(s), ph) || !mbar_wait_cl(pfull(s), ph) ||
+                        *(volatile int *)&s_abort) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(smem + s * kStageBytes);
+                    const uint64_t ad = sw128_desc(sa), bd = sw128_desc(sa + kABytes);
+#pragma unroll
+                    for (int k = 0; k < kBK / 16; k++)
+                        mma_bf16_pair(d_tmem, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), kIdesc,
+                                      (kb | k) != 0);
+                    mma_commit_pair(empty(s));
+                    mma_commit_pair(peer_addr(empty(s), 1));
+                }
+                if (ok) {
+                    mma_commit_pair(tfull(acc));
+                    mma_commit_pair(peer_addr(tfull(acc), 1));
+                }
+            }
+            if (!ok) s_abort = 1;
+        }
+    } else {
+        // ---- epilogue: this CTA's 128 accumulator rows -> softcap -> global
+        const int q = warp & 3;
+        const uint32_t tempty0 = peer_addr(tempty(0), 0), tempty1 = peer_addr(tempty(1), 0);
+        int local = 0;
+        for (int tile = pair; tile < n_tiles; tile += n_pairs, local++) {
+            const int acc = local & 1;
+            const uint32_t aph = (uint32_t)(local >> 1) & 1u;
+            if (!mbar_wait(tfull(acc), aph)) {
+                s_abort = 1;
+                break;
+            }
+            if (*(volatile int *)&s_abort) break;
+            tc_fence_after();
+            const int mt = tile % tiles_m2, nt = tile / tiles_m2;
+            const int row = mt * 2 * kBM + (int)rank * kBM + 32 * q + lane;
+            float *orow = args.out + (size_t)row * (size_t)(args.n_cb * args.vocab) +
+                          (size_t)nt * BN;
+            const float cap = args.softcap;
+#pragma unroll 1
+            for (int ch = 0; ch < BN / 32; ch++) {
+                uint32_t r[32];
+                tmem_ld32(tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BN + 32 * ch), r);
+                if (row < args.batch) {
+                    float4 *dst = reinterpret_cast<float4 *>(orow + 32 * ch);
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        float o[4];
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            const float l = __uint_as_float(r[4 * i + e]);
+                            o[e] = cap > 0.0f ? cap * tanhf(l / cap) : l;
+                        }
+                        dst[i] = make_float4(o[0], o[1], o[2], o[3]);
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive_cluster(acc ? tempty1 : tempty0);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();    // the pair is done with both CTAs' TMEM and barriers
+    tc_fence_after();
+    if (warp == 1)
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                     "r"(kTmemCols)
+                     : "memory");
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -375,6 +666,50 @@ bool make_map(CUtensorMap *m, const void *base, uint64_t rows, uint64_t cols, ui
                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
            CUDA_SUCCESS;
+}
+
+template <int STAGES>
+cudaError_t launch_pair(const HeadArgs &a, const CUtensorMap &ma, int tiles_m, int sms,
+                        cudaStream_t stream)
+{
+    static bool attr[64] = {false};
+    static int pairs_cap[64] = {0};   // clusters of two that fit at once
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const size_t smem = (size_t)STAGES * (kBM + 128) * kBK * 2 + 1024 + 512;
+    if (dev < 64 && !attr[dev]) {
+        e = cudaFuncSetAttribute(head_tc2_kernel<STAGES>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * (sms / 2));
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = smem;
+        int n = 0;
+        e = cudaOccupancyMaxActiveClusters(&n, head_tc2_kernel<STAGES>, &cfg);
+        if (e != cudaSuccess) return e;
+        pairs_cap[dev] = n > 0 ? n : 1;
+        attr[dev] = true;
+    }
+    CUtensorMap mb;   // each CTA of a pair loads 128 of the tile's 256 weight rows
+    if (!make_map(&mb, a.W, (uint64_t)a.n_cb * a.rows_per_cb, (uint64_t)a.dim, 128))
+        return cudaErrorInvalidValue;
+    TcArgs t;
+    t.batch = a.batch;
+    t.n_cb = a.n_cb;
+    t.vocab = a.vocab;
+    t.rows_per_cb = a.rows_per_cb;
+    t.dim = a.dim;
+    t.tiles_m = tiles_m;
+    t.tiles_n = a.n_cb * (a.vocab / 256);
+    t.n_tiles = ((tiles_m + 1) / 2) * t.tiles_n;
+    t.softcap = a.softcap;
+    t.out = a.out;
+    const int pairs = dev < 64 ? pairs_cap[dev] : 1;
+    const int grid = 2 * (t.n_tiles < pairs ? t.n_tiles : pairs);
+    head_tc2_kernel<STAGES><<<grid, kThreads, smem, stream>>>(ma, mb, t);
+    return cudaGetLastError();
 }
 
 template <int BN, int STAGES>
@@ -430,6 +765,9 @@ cudaError_t launch_head_tc_bf16(const HeadArgs &a, cudaStream_t stream)
     const int tiles_m = (a.batch + kBM - 1) / kBM;
     // the widest N tile that still gives every SM work
     const int cols = a.n_cb * a.vocab;
+    // two-SM pairs once every pair has a 256 x 256 tile
+    if (a.vocab % 256 == 0 && ((tiles_m + 1) / 2) * (cols / 256) >= sms / 2)
+        return launch_pair<6>(a, ma, tiles_m, sms, stream);
     if (a.vocab % 256 == 0 && tiles_m * (cols / 256) >= sms)
         return launch_bn<256, 4>(a, ma, tiles_m, sms, stream);
     if (a.vocab % 128 == 0 && tiles_m * (cols / 128) >= sms)
