@@ -387,6 +387,17 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr)
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
                  : "memory");
 }
+// TMA load into this CTA's shared memory, completing on the mbarrier at cluster
+// address `bar` (in either CTA of the pair).  Not a multicast.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap *map, int x, int y,
+                                                 uint32_t bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
 __device__ __forceinline__ void cluster_sync()
 {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
@@ -417,14 +428,15 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t bar)
 // shared memory and half of the accumulator rows in its own TMEM.  Per SM and
 // 64-deep K step that is 32 KB of operands instead of 48 KB for the same MMA
 // work, which is what limits the one-SM kernel (its operands come from L2).
-//   warp 0 (both CTAs)   TMA producer of the CTA's halves, on its own `full`;
-//   warp 1, rank 0       issues the pair's MMAs once both halves are in: its
-//                        own `full`, and `pfull`, where warp 1 of rank 1
-//                        forwards the completion of rank 1's `full`;
-//                        commits release `empty` and signal `tfull` in both CTAs;
-//   warps 2..5 (both)    epilogue of the CTA's 128 accumulator rows, then an
-//                        arrive on rank 0's `tempty` (256 arrivals).
-// No load is multicast: every copy lands in the CTA that issued it.
+//   warp 0 (both CTAs)   TMA producer of the CTA's halves; both CTAs' copies
+//                        complete on rank 0's `full`, which expects both;
+//   warp 1, rank 0       issues the pair's MMAs; its commits release `empty`
+//                        and signal `tfull` in both CTAs;
+//   warps 2..5 (both)    epilogue of the CTA's 128 accumulator rows, then one
+//                        arrive per warp on rank 0's `tempty` (8 arrivals).
+// No load is multicast: every copy lands in the CTA that issued it.  A CTA that
+// gives up waits at the final cluster barrier, so its shared memory outlives
+// any copy of its own still in flight while rank 0 drains `full`.
 template <int STAGES>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     head_tc2_kernel(const __grid_constant__ CUtensorMap map_a,
@@ -442,8 +454,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     unsigned char *smem = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * kStageBytes);
-    // bars: full[STAGES], empty[STAGES], tfull[2], tempty[2], pfull[STAGES]; the TMEM slot
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * STAGES + 4);
+    // bars: full[STAGES], empty[STAGES], tfull[2], tempty[2]; the TMEM slot
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 4);
     __shared__ int s_abort;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -453,18 +465,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     auto empty = [&](int s) { return smem_u32(bars + STAGES + s); };
     auto tfull = [&](int a) { return smem_u32(bars + 2 * STAGES + a); };
     auto tempty = [&](int a) { return smem_u32(bars + 2 * STAGES + 2 + a); };
-    auto pfull = [&](int s) { return smem_u32(bars + 2 * STAGES + 4 + s); };
 
     if (threadIdx.x == 0) {
         s_abort = 0;
         for (int s = 0; s < STAGES; s++) {
             mbar_init(full(s), 1);
             mbar_init(empty(s), 1);
-            mbar_init(pfull(s), 1);
         }
         for (int a = 0; a < 2; a++) {
             mbar_init(tfull(a), 1);
-            mbar_init(tempty(a), 256);
+            mbar_init(tempty(a), 8);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -507,42 +517,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         break;
                     }
                     const uint32_t sa = smem_u32(smem + s * kStageBytes);
-                    mbar_expect_tx(full(s), kStageBytes);
-                    tma_load_2d(sa, &map_a, kb * kBK, a_row, full(s));
-                    tma_load_2d(sa + kABytes, &map_b, kb * kBK, b_row, full(s));
+                    if (rank == 0) mbar_expect_tx(full(s), 2 * kStageBytes);   // both halves
+                    const uint32_t fb = peer_addr(full(s), 0);   // rank 0's, as a cluster address
+                    tma_load_2d_pair(sa, &map_a, kb * kBK, a_row, fb);
+                    tma_load_2d_pair(sa + kABytes, &map_b, kb * kBK, b_row, fb);
                 }
             }
             if (!ok) {
                 s_abort = 1;
-                // this CTA's copies still in flight land before it leaves
-                for (int k = 0; k < STAGES && k < it; k++) {
-                    const int j = it - 1 - k;
-                    mbar_wait(full(j % STAGES), (uint32_t)(j / STAGES) & 1u);
-                }
-            }
-        }
-    } else if (warp == 1 && rank == 1) {
-        // ---- forwards "stage s of rank 1 is in" to rank 0's pfull(s)
-        if (lane == 0) {
-            int it = 0;
-            for (int tile = pair; tile < n_tiles; tile += n_pairs) {
-                bool ok = true;
-                for (int kb = 0; kb < KB; kb++, it++) {
-                    const int s = it % STAGES;
-                    const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
-                    if (!mbar_wait(full(s), ph) || *(volatile int *)&s_abort) {
-                        ok = false;
-                        break;
+                if (rank == 0)   // the pair's copies still in flight land first
+                    for (int k = 0; k < STAGES && k < it; k++) {
+                        const int j = it - 1 - k;
+                        mbar_wait(full(j % STAGES), (uint32_t)(j / STAGES) & 1u);
                     }
-                    mbar_arrive_cluster(peer_addr(pfull(s), 0));
-                }
-                if (!ok) {
-                    s_abort = 1;
-                    break;
-                }
             }
         }
-    } else if (warp == 1) {
+    } else if (warp == 1 && rank == 0) {
         // ---- MMA issuer (rank 0) for the pair
         if (lane == 0) {
             int it = 0, local = 0;
@@ -559,8 +549,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 for (int kb = 0; kb < KB; kb++, it++) {
                     const int s = it % STAGES;
                     const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
-                    if (!mbar_wait(full(s), ph) || !mbar_wait_cl(pfull(s), ph) ||
-                        *(volatile int *)&s_abort) {
+                    if (!mbar_wait_cl(full(s), ph) || *(volatile int *)&s_abort) {
                         ok = false;
                         break;
                     }
@@ -581,7 +570,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
             if (!ok) s_abort = 1;
         }
-    } else {
+    } else if (warp >= 2) {
         // ---- epilogue: this CTA's 128 accumulator rows -> softcap -> global
         const int q = warp & 3;
         const uint32_t tempty0 = peer_addr(tempty(0), 0), tempty1 = peer_addr(tempty(1), 0);
@@ -619,7 +608,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 }
             }
             tc_fence_before();
-            mbar_arrive_cluster(acc ? tempty1 : tempty0);
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(acc ? tempty1 : tempty0);
         }
     }
 
