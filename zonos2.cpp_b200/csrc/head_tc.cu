@@ -13,7 +13,8 @@
 //               one elected lane, accumulating a 128 x BN f32 tile in TMEM;
 //               two accumulators alternate so the epilogue of one tile
 //               overlaps the MMAs of the next;
-//   warps 2..5  epilogue: tcgen05.ld of their 32 TMEM lanes, softcap, f32 store.
+//   warps 2..9  epilogue: tcgen05.ld of their 32 TMEM lanes (two warps per lane
+//               quarter, each half of the columns), softcap, f32 store.
 // Stages hand over through mbarriers: TMA completes `full`, tcgen05.commit
 // releases `empty` and signals `tfull`, the epilogue releases `tempty`.
 // Every wait is bounded: after ~2 s it records an error in g_device_error and
@@ -48,7 +49,8 @@ namespace {
 
 constexpr int kBM = 128;            // rows of hidden per tile (TMEM lanes)
 constexpr int kBK = 64;             // bf16 elements per 128-byte swizzled row
-constexpr int kThreads = 192;       // 6 warps
+constexpr int kThreads = 320;       // 10 warps: producer, MMA, 8 epilogue
+constexpr int kEpiThreads = 256;
 constexpr unsigned long long kWaitNs = 2000000000ull;
 
 enum : int { kErrTimeout = 1 };
@@ -162,6 +164,17 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32])
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// cap * tanh(l / cap) as cap - 2 cap / (2^(l k2) + 1), k2 = 2 log2(e) / cap, with
+// the hardware exp2 and reciprocal approximations (relative errors near 2^-22):
+// within 2e-6 absolute of the exact softcap for cap = 15; saturates to +-cap.
+__device__ __forceinline__ float softcap_fast(float l, float cap, float k2)
+{
+    float e, r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(l * k2));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(e + 1.0f));
+    return __fmaf_rn(-2.0f * cap, r, cap);
+}
+
 struct TcArgs {
     int batch, n_cb, vocab, rows_per_cb, dim;
     int tiles_m, tiles_n, n_tiles;
@@ -206,7 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int a = 0; a < 2; a++) {
             mbar_init(tfull(a), 1);
-            mbar_init(tempty(a), 128);
+            mbar_init(tempty(a), kEpiThreads);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -295,6 +308,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         // ---- epilogue: TMEM -> softcap -> global
         const int q = warp & 3;   // the TMEM lane quarter this warp may read
+        const int half = (warp - 2) >> 2;   // which half of the tile's columns
         int local = 0;
         for (int tile = blockIdx.x; tile < args.n_tiles; tile += gridDim.x, local++) {
             const int acc = local & 1;
@@ -310,8 +324,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             float *orow = args.out + (size_t)row * (size_t)(args.n_cb * args.vocab) +
                           (size_t)nt * BN;
             const float cap = args.softcap;
+            const float k2 = 2.0f * 1.4426950408889634f / cap;   // 2 log2(e) / cap
 #pragma unroll 1
-            for (int ch = 0; ch < BN / 32; ch++) {
+            for (int ch = half * (BN / 64); ch < (half + 1) * (BN / 64); ch++) {
                 uint32_t r[32];
                 tmem_ld32(tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BN + 32 * ch), r);
                 if (row < args.batch) {
@@ -322,7 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                         for (int e = 0; e < 4; e++) {
                             const float l = __uint_as_float(r[4 * i + e]);
-                            o[e] = cap > 0.0f ? cap * tanhf(l / cap) : l;
+                            o[e] = cap > 0.0f ? softcap_fast(l, cap, k2) : l;
                         }
                         dst[i] = make_float4(o[0], o[1], o[2], o[3]);
                     }
@@ -474,7 +489,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         for (int a = 0; a < 2; a++) {
             mbar_init(tfull(a), 1);
-            mbar_init(tempty(a), 8);
+            mbar_init(tempty(a), 2 * kEpiThreads / 32);   // one per epilogue warp, both CTAs
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -572,7 +587,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
     } else if (warp >= 2) {
         // ---- epilogue: this CTA's 128 accumulator rows -> softcap -> global
-        const int q = warp & 3;
+        const int q = warp & 3;             // the TMEM lane quarter this warp may read
+        const int half = (warp - 2) >> 2;   // which half of the tile's columns
         const uint32_t tempty0 = peer_addr(tempty(0), 0), tempty1 = peer_addr(tempty(1), 0);
         int local = 0;
         for (int tile = pair; tile < n_tiles; tile += n_pairs, local++) {
@@ -589,8 +605,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             float *orow = args.out + (size_t)row * (size_t)(args.n_cb * args.vocab) +
                           (size_t)nt * BN;
             const float cap = args.softcap;
+            const float k2 = 2.0f * 1.4426950408889634f / cap;   // 2 log2(e) / cap
 #pragma unroll 1
-            for (int ch = 0; ch < BN / 32; ch++) {
+            for (int ch = half * (BN / 64); ch < (half + 1) * (BN / 64); ch++) {
                 uint32_t r[32];
                 tmem_ld32(tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BN + 32 * ch), r);
                 if (row < args.batch) {
@@ -601,7 +618,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
                         for (int e = 0; e < 4; e++) {
                             const float l = __uint_as_float(r[4 * i + e]);
-                            o[e] = cap > 0.0f ? cap * tanhf(l / cap) : l;
+                            o[e] = cap > 0.0f ? softcap_fast(l, cap, k2) : l;
                         }
                         dst[i] = make_float4(o[0], o[1], o[2], o[3]);
                     }
