@@ -165,8 +165,10 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32])
 }
 
 // cap * tanh(l / cap) as cap - 2 cap / (2^(l k2) + 1), k2 = 2 log2(e) / cap, with
-// the hardware exp2 and reciprocal approximations (relative errors near 2^-22):
-// within 2e-6 absolute of the exact softcap for cap = 15; saturates to +-cap.
+// the hardware exp2 and reciprocal approximations (relative errors of about
+// 2^-22 and 2^-23): the reciprocal r <= 1 is off by about 2^-21 relative, so
+// the result is within 2 cap 2^-21 (1.5e-5 for cap = 15) of the exact softcap,
+// far inside the bf16 path's tolerance; it saturates to +-cap.
 __device__ __forceinline__ float softcap_fast(float l, float cap, float k2)
 {
     float e, r;
