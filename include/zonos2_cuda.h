@@ -173,6 +173,20 @@ int zonos2cu_get_rng(zonos2cu_ctx *ctx, uint64_t *state_host);
 /* Allow bitmask [n_streams][ceil(vocab/32)]; NULL clears it. */
 int zonos2cu_set_allow(zonos2cu_ctx *ctx, const uint32_t *bits_host);
 
+/* The output RMSNorm ahead of the head in zonos2cu_ctx_step: replaces
+ * rms_norm_per_token(x, dim, n, eps, out_norm.weight) applied to the last hidden
+ * states before the multi_output head (src/zonos2_model.cpp:684-685, :19-35).
+ * With it enabled, ctx_step takes the un-normalised hidden states.  weight_host
+ * is [dim] f32, or NULL for no scale weight; enable = 0 turns it off. */
+int zonos2cu_set_out_norm(zonos2cu_ctx *ctx, int enable, const float *weight_host, float eps);
+/* Classifier-free guidance in zonos2cu_ctx_step: the blend
+ * uncond + scale * (cond - uncond) of softcapped logits that the reference
+ * applies to its prefill logits (src/zonos2_generate.cpp:157-183), here on every
+ * step.  With it enabled, ctx_step and ctx_step_host take [2*n_streams][dim]
+ * hidden states, row 2s the conditional and row 2s+1 the unconditional state
+ * of stream s; logits and codes stay [n_streams][...].  enable = 0 turns it off. */
+int zonos2cu_set_cfg(zonos2cu_ctx *ctx, int enable, float scale);
+
 /* One sampling step from device logits [n_streams][n_cb][row_stride] on
  * `stream` (NULL = the legacy default stream, like every "_dev" call); the
  * history position advances by one (mod hist_len) on success.  The host-path
@@ -187,8 +201,9 @@ int zonos2cu_ctx_sample(zonos2cu_ctx *ctx, const float *logits_dev, long long ro
 int zonos2cu_ctx_sample_host(zonos2cu_ctx *ctx, const float *logits_host, long long row_stride,
                              const zonos2cu_sample_params *params, int delay_step,
                              int32_t *codes_host, int32_t *flags_host);
-/* One fused step: hidden [n_streams][dim] (device, dtype) -> head + softcap ->
- * sampler.  logits_out_dev ([n_streams][n_cb][vocab] f32) may be NULL. */
+/* One fused step: hidden [n_streams][dim] (device, dtype; [2*n_streams][dim] with
+ * guidance on) -> output RMSNorm if set -> head + softcap -> guidance blend if
+ * set -> sampler.  logits_out_dev ([n_streams][n_cb][vocab] f32) may be NULL. */
 int zonos2cu_ctx_step(zonos2cu_ctx *ctx, const void *hidden_dev, zonos2cu_dtype dtype,
                       const zonos2cu_sample_params *params, int delay_step, int32_t *codes_dev,
                       int32_t *flags_dev, float *logits_out_dev, void *stream);

@@ -101,6 +101,8 @@ class Oracle:
         L.orc_step.restype = C.c_int
         L.orc_head_softcap.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p,
                                        C.c_int, C.c_float, C.c_void_p, C.c_int]
+        L.orc_out_norm.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_float, C.c_void_p]
+        L.orc_cfg_blend.argtypes = [C.c_void_p, C.c_void_p, C.c_long, C.c_float, C.c_void_p]
 
     # generator -------------------------------------------------------------
     def rng_seed(self, seed: int) -> np.ndarray:
@@ -162,6 +164,20 @@ class Oracle:
                                 nthreads)
         return out
 
+    def out_norm(self, x, eps=1e-5, weight=None):
+        """rms_norm_per_token over the rows of x ([n, dim] f32); returns a copy."""
+        x = np.array(x, np.float32, copy=True, order="C")
+        w = None if weight is None else np.ascontiguousarray(weight, np.float32)
+        self.L.orc_out_norm(_p(x), x.shape[-1], x.size // x.shape[-1], eps, _p(w))
+        return x
+
+    def cfg_blend(self, cond, uncond, scale):
+        cond = np.ascontiguousarray(cond, np.float32)
+        uncond = np.ascontiguousarray(uncond, np.float32)
+        out = np.empty_like(cond)
+        self.L.orc_cfg_blend(_p(cond), _p(uncond), cond.size, scale, _p(out))
+        return out
+
 
 class Reference:
     """The reference's own sources, compiled unmodified (oracle/_ref)."""
@@ -185,6 +201,7 @@ class Reference:
                                          C.c_void_p]
         L.ref_head_softcap.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p,
                                        C.c_int, C.c_float, C.c_void_p, C.c_int]
+        L.ref_out_norm.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_float, C.c_void_p]
         L.ref_step.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_long, C.c_float, C.c_int,
                                C.c_float, C.c_float, C.c_float, C.c_int, C.POINTER(C.c_uint64),
                                C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_int,
@@ -216,6 +233,12 @@ class Reference:
         self.L.ref_head_softcap(_p(W), rows_per_cb, n_cb, vocab, D, _p(h), B, softcap, _p(out),
                                 nthreads)
         return out
+
+    def out_norm(self, x, eps=1e-5, weight=None):
+        x = np.array(x, np.float32, copy=True, order="C")
+        w = None if weight is None else np.ascontiguousarray(weight, np.float32)
+        self.L.ref_out_norm(_p(x), x.shape[-1], x.size // x.shape[-1], eps, _p(w))
+        return x
 
     def step(self, logits, params: Params, rng, hist=None, hist_pos=0, allow=None, delay_step=-1,
              nthreads=0, row_stride=None):

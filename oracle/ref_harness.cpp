@@ -70,6 +70,12 @@ void ref_linear_forward(const float *W, int in_f, int out_f, const float *x, int
     linear_forward(W, in_f, out_f, x, n_tok, out);
 }
 
+/* The reference's own rms_norm_per_token, in place (weight may be NULL). */
+void ref_out_norm(float *x, int dim, int n_rows, float eps, const float *weight)
+{
+    rms_norm_per_token(x, dim, n_rows, eps, weight);
+}
+
 /* W: [n_cb*rows_per_cb, dim]; out: [batch][n_cb][vocab] (the sampled rows). */
 void ref_head_softcap(const float *W, int rows_per_cb, int n_cb, int vocab, int dim,
                       const float *h, int batch, float softcap, float *out, int nthreads)

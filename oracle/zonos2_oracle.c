@@ -284,3 +284,30 @@ void orc_head_softcap(const float *W, int rows_per_cb, int n_cb, int vocab, int 
             }
         }
 }
+
+
+/* The output RMSNorm applied to the hidden states before the head
+ * (src/zonos2_model.cpp:684-685 calling rms_norm_per_token, :19-35): per row,
+ * the f32 sum of squares in index order, rms = sqrt(ss / dim + eps), rcp =
+ * 1 / rms, then x * rcp (times the scale weight when there is one).  In place. */
+void orc_out_norm(float *x, int dim, int n_rows, float eps, const float *weight)
+{
+    for (int t = 0; t < n_rows; t++) {
+        float *xt = x + (size_t)t * (size_t)dim;
+        float ss = 0.0f;
+        for (int d = 0; d < dim; d++) ss += xt[d] * xt[d];
+        const float rms = sqrtf(ss / (float)dim + eps);
+        const float rcp = 1.0f / rms;
+        if (weight)
+            for (int d = 0; d < dim; d++) xt[d] = xt[d] * rcp * weight[d];
+        else
+            for (int d = 0; d < dim; d++) xt[d] *= rcp;
+    }
+}
+
+/* Classifier-free guidance on softcapped logits, as the reference blends its
+ * prefill logits (src/zonos2_generate.cpp:178-183): out = u + s * (c - u). */
+void orc_cfg_blend(const float *cond, const float *uncond, long n, float scale, float *out)
+{
+    for (long i = 0; i < n; i++) out[i] = uncond[i] + scale * (cond[i] - uncond[i]);
+}

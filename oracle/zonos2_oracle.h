@@ -84,6 +84,14 @@ int orc_step(const float *logits, int n_streams, int n_cb, int vocab, long row_s
 void orc_head_softcap(const float *W, int rows_per_cb, int n_cb, int vocab, int dim,
                       const float *h, int batch, float softcap, float *out, int nthreads);
 
+/* rms_norm_per_token (src/zonos2_model.cpp:19-35) over n_rows rows, in place;
+ * weight may be NULL. */
+void orc_out_norm(float *x, int dim, int n_rows, float eps, const float *weight);
+
+/* out = uncond + scale * (cond - uncond), element by element
+ * (src/zonos2_generate.cpp:178-183). */
+void orc_cfg_blend(const float *cond, const float *uncond, long n, float scale, float *out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -141,3 +141,27 @@ def test_restatement_step_matches_reference_harness(oracle):
         assert (f1 == f2).all()
         hist2[:] = hist          # continue both from the same state
     assert (rng == rng2).all()
+
+
+@pytest.mark.skipif(not ref_available, reason="oracle/_ref not built")
+@pytest.mark.parametrize("dim,rows", [(2048, 9), (37, 5)])
+def test_out_norm_pinned_to_reference(oracle, dim, rows):
+    """The restated output RMSNorm equals the reference's own rms_norm_per_token
+    (compiled unmodified), bit for bit, with and without a scale weight."""
+    R = Reference()
+    rs = np.random.default_rng(dim + rows)
+    x = rs.normal(0, 3, (rows, dim)).astype(np.float32)
+    w = rs.normal(1, 0.2, dim).astype(np.float32)
+    for weight in (w, None):
+        a = oracle.out_norm(x, 1e-5, weight)
+        b = R.out_norm(x, 1e-5, weight)
+        assert (a.view(np.uint32) == b.view(np.uint32)).all()
+
+
+def test_cfg_blend_formula(oracle):
+    rs = np.random.default_rng(3)
+    c = rs.normal(0, 4, 1000).astype(np.float32)
+    u = rs.normal(0, 4, 1000).astype(np.float32)
+    s = np.float32(1.7)
+    want = (u + s * (c - u)).astype(np.float32)   # float32 numpy: one rounding per op
+    assert (oracle.cfg_blend(c, u, s) == want).all()

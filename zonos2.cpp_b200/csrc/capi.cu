@@ -211,15 +211,23 @@ int zonos2cu_sample_token(uint64_t rng_state[4], const float *logits, int vocab_
     return out[0];
 }
 
-int zonos2cu_head_softcap(const void *W_dev, zonos2cu_dtype dtype, int rows_per_cb, int n_cb,
-                          int vocab, int dim, const void *hidden_dev, int batch, float softcap,
-                          float *logits_dev, void *stream)
+}  // extern "C"
+
+namespace {
+
+// The head on `batch` hidden rows; with cfg, rows pair up and `logits_dev` gets
+// batch / 2 blended rows.
+int launch_head(const void *W_dev, zonos2cu_dtype dtype, int rows_per_cb, int n_cb, int vocab,
+                int dim, const void *hidden_dev, int batch, float softcap, float *logits_dev,
+                void *stream, bool cfg, float cfg_scale)
 {
     if (n_cb < 1 || vocab < 1 || dim < 1 || batch < 0 || rows_per_cb < vocab)
         return ZONOS2CU_EINVAL;
     if (isnan(softcap)) return ZONOS2CU_EINVAL;
     if (batch > 0 && (!W_dev || !hidden_dev || !logits_dev)) return ZONOS2CU_EINVAL;
     z2::HeadArgs a{W_dev, rows_per_cb, n_cb, vocab, dim, hidden_dev, batch, softcap, logits_dev};
+    a.cfg = cfg ? 1 : 0;
+    a.cfg_scale = cfg_scale;
     cudaError_t e;
     if (dtype == ZONOS2CU_F32) {
         e = z2::launch_head_gemv_f32(a, (cudaStream_t)stream);
@@ -231,6 +239,18 @@ int zonos2cu_head_softcap(const void *W_dev, zonos2cu_dtype dtype, int rows_per_
     }
     if (e != cudaSuccess) return cuda_fail(e, "head launch");
     return ZONOS2CU_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int zonos2cu_head_softcap(const void *W_dev, zonos2cu_dtype dtype, int rows_per_cb, int n_cb,
+                          int vocab, int dim, const void *hidden_dev, int batch, float softcap,
+                          float *logits_dev, void *stream)
+{
+    return launch_head(W_dev, dtype, rows_per_cb, n_cb, vocab, dim, hidden_dev, batch, softcap,
+                       logits_dev, stream, false, 1.0f);
 }
 
 int zonos2cu_device_error(void)
@@ -261,6 +281,15 @@ struct zonos2cu_ctx {
     void *head = nullptr;        // [C*V][D] of head_dtype
     zonos2cu_dtype head_dtype = ZONOS2CU_F32;
     float *logits = nullptr;     // [S][C][V] fused-step intermediate
+    // output RMSNorm ahead of the head (zonos2cu_set_out_norm)
+    bool norm_on = false;
+    float norm_eps = 1e-5f;
+    float *norm_w = nullptr;     // [D] or unused
+    bool norm_has_w = false;
+    void *normed = nullptr;      // [2S][D] of the head's type: the normalised rows
+    // classifier-free guidance (zonos2cu_set_cfg): steps take 2S hidden rows
+    bool cfg_on = false;
+    float cfg_scale = 1.0f;
     // host-path staging, grown on demand
     float *in_logits = nullptr;
     size_t in_logits_bytes = 0;
@@ -376,6 +405,8 @@ int zonos2cu_ctx_destroy(zonos2cu_ctx *c)
     cudaFree(c->allow);
     cudaFree(c->head);
     cudaFree(c->logits);
+    cudaFree(c->norm_w);
+    cudaFree(c->normed);
     cudaFree(c->in_logits);
     cudaFree(c->in_hidden);
     cudaFree(c->out);
@@ -494,6 +525,41 @@ int zonos2cu_set_allow(zonos2cu_ctx *c, const uint32_t *bits_host)
     return ZONOS2CU_OK;
 }
 
+int zonos2cu_set_out_norm(zonos2cu_ctx *c, int enable, const float *weight_host, float eps)
+{
+    if (!c || c->dims.dim < 1) return ZONOS2CU_EINVAL;
+    if (enable && (!(eps >= 0.0f) || !isfinite(eps))) return ZONOS2CU_EINVAL;
+    DeviceGuard g(c->device);
+    Z2_CK(cudaDeviceSynchronize());   // no step may still be using the state
+    if (!enable) {
+        c->norm_on = false;
+        return ZONOS2CU_OK;
+    }
+    const size_t D = (size_t)c->dims.dim;
+    if (!c->normed && n_rows(c))   // room for 2S rows of f32 covers every mode
+        Z2_CK(cudaMalloc(&c->normed, sizeof(float) * 2 * (size_t)c->dims.n_streams * D));
+    if (weight_host) {
+        if (!c->norm_w) Z2_CK(cudaMalloc(&c->norm_w, sizeof(float) * D));
+        Z2_CK(cudaMemcpyAsync(c->norm_w, weight_host, sizeof(float) * D, cudaMemcpyHostToDevice,
+                              c->stream));
+        Z2_CK(cudaStreamSynchronize(c->stream));
+    }
+    c->norm_has_w = weight_host != nullptr;
+    c->norm_eps = eps;
+    c->norm_on = true;
+    return ZONOS2CU_OK;
+}
+
+int zonos2cu_set_cfg(zonos2cu_ctx *c, int enable, float scale)
+{
+    if (!c || (enable && !isfinite(scale))) return ZONOS2CU_EINVAL;
+    DeviceGuard g(c->device);
+    Z2_CK(cudaDeviceSynchronize());   // no step may still be using the state
+    c->cfg_on = enable != 0;
+    c->cfg_scale = scale;
+    return ZONOS2CU_OK;
+}
+
 int zonos2cu_ctx_sample(zonos2cu_ctx *c, const float *logits_dev, long long row_stride,
                         const zonos2cu_sample_params *params, int delay_step, int32_t *codes_dev,
                         int32_t *flags_dev, void *stream)
@@ -554,8 +620,15 @@ int zonos2cu_ctx_step(zonos2cu_ctx *c, const void *hidden_dev, zonos2cu_dtype dt
     if (rc) return rc;
     cudaStream_t st = (cudaStream_t)stream;
     float *lg = logits_out_dev ? logits_out_dev : c->logits;
-    rc = zonos2cu_head_softcap(c->head, dtype, d.vocab, d.n_cb, d.vocab, d.dim, hidden_dev,
-                               d.n_streams, 15.0f, lg, st);
+    const int rows_in = (c->cfg_on ? 2 : 1) * d.n_streams;
+    const void *h = hidden_dev;
+    if (c->norm_on && rows_in > 0) {   // rms_norm_per_token (src/zonos2_model.cpp:684-685)
+        Z2_CK(z2::launch_out_norm(hidden_dev, dtype == ZONOS2CU_BF16, rows_in, d.dim, c->norm_eps,
+                                  c->norm_has_w ? c->norm_w : nullptr, c->normed, st));
+        h = c->normed;
+    }
+    rc = launch_head(c->head, dtype, d.vocab, d.n_cb, d.vocab, d.dim, h, rows_in, 15.0f, lg, st,
+                     c->cfg_on, c->cfg_scale);
     if (rc) return rc;
     return zonos2cu_ctx_sample(c, lg, d.vocab, params, delay_step, codes_dev, flags_dev, st);
 }
@@ -569,7 +642,8 @@ int zonos2cu_ctx_step_host(zonos2cu_ctx *c, const void *hidden_host, zonos2cu_dt
     DeviceGuard g(c->device);
     const size_t rows = n_rows(c);
     if (rows == 0) return ZONOS2CU_OK;
-    const size_t bytes = (dtype == ZONOS2CU_F32 ? 4 : 2) * (size_t)c->dims.n_streams * c->dims.dim;
+    const size_t bytes = (dtype == ZONOS2CU_F32 ? 4 : 2) * (size_t)(c->cfg_on ? 2 : 1) *
+                         (size_t)c->dims.n_streams * c->dims.dim;
     int rc = grow(&c->in_hidden, &c->in_hidden_bytes, bytes);
     if (rc) return rc;
     if ((rc = ensure_out(c))) return rc;

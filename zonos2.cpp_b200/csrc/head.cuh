@@ -12,8 +12,19 @@ struct HeadArgs {
     const void *hidden;   // [batch][dim]
     int batch;
     float softcap;        // <= 0: no cap
-    float *out;           // [batch][n_cb][vocab] f32
+    float *out;           // [batch][n_cb][vocab] f32, or [batch/2][..] with cfg
+    // Classifier-free guidance: hidden rows come in pairs (2s conditional,
+    // 2s+1 unconditional) and out row s is u + cfg_scale * (c - u) of the two
+    // softcapped rows (src/zonos2_generate.cpp:178-183).  batch is even.
+    int cfg = 0;
+    float cfg_scale = 1.0f;
 };
+
+// The output RMSNorm of rows x [rows][dim] (f32, or bf16 when `bf16`) into y of
+// the same type, with the optional f32 scale weight w [dim]
+// (head_prologue.cu).
+cudaError_t launch_out_norm(const void *x, bool bf16, int rows, int dim, float eps,
+                            const float *w, void *y, cudaStream_t stream);
 
 // f32 weights and hidden states: one warp per output row, f64 accumulation
 // (head_gemv.cu).

@@ -7,7 +7,9 @@
 // from HBM by one warp with coalesced 128-bit loads (the bound is the
 // 4*n_cb*vocab*dim bytes of W), and the dot product is accumulated in f64 so
 // the f32 result is the correctly rounded dot product -- within the
-// reference's own sequential-f32 rounding error of its value.
+// reference's own sequential-f32 rounding error of its value.  With
+// classifier-free guidance, rows 2s and 2s+1 (conditional, unconditional) are
+// blended into output row s after the softcap (src/zonos2_generate.cpp:178-183).
 #include <math.h>
 
 #include "common.cuh"
@@ -22,13 +24,14 @@ constexpr int kGemvWarps = 8;
 __global__ void __launch_bounds__(32 * kGemvWarps)
     head_gemv_f32_kernel(const float *__restrict__ W, int rows_per_cb, int n_cb, int vocab,
                          int dim, const float *__restrict__ hid, int batch, float cap,
-                         float *__restrict__ out, int vec)
+                         float *__restrict__ out, int vec, int cfg, float cfg_scale)
 {
     const int lane = threadIdx.x & 31;
     const int o = blockIdx.x * kGemvWarps + (threadIdx.x >> 5);
     if (o >= n_cb * vocab) return;
     const int c = o / vocab, v = o - c * vocab;
     const float *w = W + ((size_t)c * rows_per_cb + v) * (size_t)dim;
+    float cond = 0.0f;   // with cfg: the softcapped logit of the pair's conditional row
     for (int b = 0; b < batch; b++) {
         const float *h = hid + (size_t)b * dim;
         double acc = 0.0;
@@ -49,7 +52,14 @@ __global__ void __launch_bounds__(32 * kGemvWarps)
         if (lane == 0) {
             float l = __double2float_rn(acc);
             if (cap > 0.0f) l = cap * tanhf(l / cap);
-            out[((size_t)b * n_cb + c) * vocab + v] = l;
+            if (!cfg) {
+                out[((size_t)b * n_cb + c) * vocab + v] = l;
+            } else if ((b & 1) == 0) {
+                cond = l;
+            } else {   // u + s * (c - u), rounded step by step like the reference
+                out[((size_t)(b >> 1) * n_cb + c) * vocab + v] =
+                    __fadd_rn(l, __fmul_rn(cfg_scale, __fsub_rn(cond, l)));
+            }
         }
     }
 }
@@ -65,7 +75,8 @@ cudaError_t launch_head_gemv_f32(const HeadArgs &a, cudaStream_t stream)
     const int blocks = (rows + kGemvWarps - 1) / kGemvWarps;
     head_gemv_f32_kernel<<<blocks, 32 * kGemvWarps, 0, stream>>>(
         static_cast<const float *>(a.W), a.rows_per_cb, a.n_cb, a.vocab, a.dim,
-        static_cast<const float *>(a.hidden), a.batch, a.softcap, a.out, vec);
+        static_cast<const float *>(a.hidden), a.batch, a.softcap, a.out, vec, a.cfg,
+        a.cfg_scale);
     return cudaGetLastError();
 }
 

@@ -181,8 +181,40 @@ struct TcArgs {
     int batch, n_cb, vocab, rows_per_cb, dim;
     int tiles_m, tiles_n, n_tiles;
     float softcap;
-    float *out;  // [batch][n_cb * vocab]
+    float *out;  // [batch][n_cb * vocab], or [batch / 2][..] with cfg
+    int cfg;     // rows 2s, 2s+1 (conditional, unconditional) blend into out row s
+    float cfg_scale;
 };
+
+// The epilogue's store of one 32-column chunk of row `row` (lane = row's lane in
+// its warp; rows 2s and 2s+1 sit in lanes of one warp): the softcap, and with
+// classifier-free guidance the blend u + s * (c - u) of the pair, taken from
+// the neighbouring lane and stored by the even lane as output row s
+// (src/zonos2_generate.cpp:178-183).
+__device__ __forceinline__ void store_chunk(const TcArgs &args, const uint32_t (&r)[32], int row,
+                                            size_t col, float k2)
+{
+    const float cap = args.softcap;
+    const size_t ld = (size_t)(args.n_cb * args.vocab);
+    const bool even = (row & 1) == 0;
+    float *dst = args.cfg ? args.out + (size_t)(row >> 1) * ld + col
+                          : args.out + (size_t)row * ld + col;
+    const bool st = row < args.batch && (!args.cfg || even);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        float o[4];
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const float l = __uint_as_float(r[4 * i + e]);
+            o[e] = cap > 0.0f ? softcap_fast(l, cap, k2) : l;
+            if (args.cfg) {
+                const float u = __shfl_xor_sync(kFull, o[e], 1);
+                o[e] = __fadd_rn(u, __fmul_rn(args.cfg_scale, __fsub_rn(o[e], u)));
+            }
+        }
+        if (st) reinterpret_cast<float4 *>(dst)[i] = make_float4(o[0], o[1], o[2], o[3]);
+    }
+}
 
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -323,27 +355,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const int mt = tile % args.tiles_m, nt = tile / args.tiles_m;
             const int row = mt * kBM + 32 * q + lane;
-            float *orow = args.out + (size_t)row * (size_t)(args.n_cb * args.vocab) +
-                          (size_t)nt * BN;
-            const float cap = args.softcap;
-            const float k2 = 2.0f * 1.4426950408889634f / cap;   // 2 log2(e) / cap
+            const float k2 = 2.0f * 1.4426950408889634f / args.softcap;   // 2 log2(e) / cap
 #pragma unroll 1
             for (int ch = half * (BN / 64); ch < (half + 1) * (BN / 64); ch++) {
                 uint32_t r[32];
                 tmem_ld32(tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BN + 32 * ch), r);
-                if (row < args.batch) {
-                    float4 *dst = reinterpret_cast<float4 *>(orow + 32 * ch);
-#pragma unroll
-                    for (int i = 0; i < 8; i++) {
-                        float o[4];
-#pragma unroll
-                        for (int e = 0; e < 4; e++) {
-                            const float l = __uint_as_float(r[4 * i + e]);
-                            o[e] = cap > 0.0f ? softcap_fast(l, cap, k2) : l;
-                        }
-                        dst[i] = make_float4(o[0], o[1], o[2], o[3]);
-                    }
-                }
+                store_chunk(args, r, row, (size_t)nt * BN + 32 * ch, k2);
             }
             tc_fence_before();
             mbar_arrive(tempty(acc));
@@ -604,27 +621,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const int mt = tile % tiles_m2, nt = tile / tiles_m2;
             const int row = mt * 2 * kBM + (int)rank * kBM + 32 * q + lane;
-            float *orow = args.out + (size_t)row * (size_t)(args.n_cb * args.vocab) +
-                          (size_t)nt * BN;
-            const float cap = args.softcap;
-            const float k2 = 2.0f * 1.4426950408889634f / cap;   // 2 log2(e) / cap
+            const float k2 = 2.0f * 1.4426950408889634f / args.softcap;   // 2 log2(e) / cap
 #pragma unroll 1
             for (int ch = half * (BN / 64); ch < (half + 1) * (BN / 64); ch++) {
                 uint32_t r[32];
                 tmem_ld32(tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BN + 32 * ch), r);
-                if (row < args.batch) {
-                    float4 *dst = reinterpret_cast<float4 *>(orow + 32 * ch);
-#pragma unroll
-                    for (int i = 0; i < 8; i++) {
-                        float o[4];
-#pragma unroll
-                        for (int e = 0; e < 4; e++) {
-                            const float l = __uint_as_float(r[4 * i + e]);
-                            o[e] = cap > 0.0f ? softcap_fast(l, cap, k2) : l;
-                        }
-                        dst[i] = make_float4(o[0], o[1], o[2], o[3]);
-                    }
-                }
+                store_chunk(args, r, row, (size_t)nt * BN + 32 * ch, k2);
             }
             tc_fence_before();
             __syncwarp();
@@ -715,6 +717,8 @@ cudaError_t launch_pair(const HeadArgs &a, const CUtensorMap &ma, int tiles_m, i
     t.n_tiles = ((tiles_m + 1) / 2) * t.tiles_n;
     t.softcap = a.softcap;
     t.out = a.out;
+    t.cfg = a.cfg;
+    t.cfg_scale = a.cfg_scale;
     const int pairs = dev < 64 ? pairs_cap[dev] : 1;
     const int grid = 2 * (t.n_tiles < pairs ? t.n_tiles : pairs);
     head_tc2_kernel<STAGES><<<grid, kThreads, smem, stream>>>(ma, mb, t);
@@ -750,6 +754,8 @@ cudaError_t launch_bn(const HeadArgs &a, const CUtensorMap &ma, int tiles_m, int
     t.n_tiles = t.tiles_m * t.tiles_n;
     t.softcap = a.softcap;
     t.out = a.out;
+    t.cfg = a.cfg;
+    t.cfg_scale = a.cfg_scale;
     const int grid = t.n_tiles < sms ? t.n_tiles : sms;
     head_tc_kernel<BN, STAGES><<<grid, kThreads, smem, stream>>>(ma, mb, t);
     return cudaGetLastError();

@@ -37,7 +37,7 @@ EXPORTS = (
     "zonos2cu_get_history", "zonos2cu_set_rng", "zonos2cu_get_rng", "zonos2cu_set_allow",
     "zonos2cu_ctx_sample", "zonos2cu_ctx_sample_host", "zonos2cu_ctx_step",
     "zonos2cu_ctx_step_host", "zonos2cu_ctx_stream", "zonos2cu_device_error",
-    "zonos2cu_step_noalloc",
+    "zonos2cu_step_noalloc", "zonos2cu_set_out_norm", "zonos2cu_set_cfg",
 )
 
 
@@ -96,6 +96,8 @@ def lib() -> C.CDLL:
         "zonos2cu_set_history": (i, [vp, vp, i]),
         "zonos2cu_get_history": (i, [vp, vp, C.POINTER(i)]),
         "zonos2cu_set_rng": (i, [vp, vp]),
+        "zonos2cu_set_out_norm": (i, [vp, i, vp, f]),
+        "zonos2cu_set_cfg": (i, [vp, i, f]),
         "zonos2cu_get_rng": (i, [vp, vp]),
         "zonos2cu_set_allow": (i, [vp, vp]),
         "zonos2cu_ctx_sample": (i, [vp, vp, ll, C.POINTER(SampleParams), i, vp, vp, vp]),
@@ -280,6 +282,17 @@ class Context:
             return
         bits = np.ascontiguousarray(bits, np.uint32)
         _check(lib().zonos2cu_set_allow(self.h, bits.ctypes.data), "set_allow")
+
+    def set_out_norm(self, weight=None, eps: float = 1e-5, enable: bool = True) -> None:
+        """The output RMSNorm ahead of the head (weight [dim] f32 or None)."""
+        w = None if weight is None else np.ascontiguousarray(weight, np.float32)
+        _check(lib().zonos2cu_set_out_norm(self.h, int(enable),
+                                           None if w is None else w.ctypes.data,
+                                           C.c_float(eps)), "set_out_norm")
+
+    def set_cfg(self, scale: float, enable: bool = True) -> None:
+        """Guidance blend; steps then take 2 * n_streams hidden rows (2s cond, 2s+1 uncond)."""
+        _check(lib().zonos2cu_set_cfg(self.h, int(enable), C.c_float(scale)), "set_cfg")
 
     def sample(self, logits, params: SampleParams, codes, flags=None, delay_step=-1,
                row_stride=None, stream=None) -> None:
