@@ -214,6 +214,51 @@ int zonos2cu_ctx_step_host(zonos2cu_ctx *ctx, const void *hidden_host, zonos2cu_
 /* The context's CUDA stream (cudaStream_t), for callers that order work on it. */
 void *zonos2cu_ctx_stream(zonos2cu_ctx *ctx);
 
+/* ---- the generation loop around the step ------------------------------------
+ * Replaces the frame bookkeeping of zonos2_generate's loop
+ * (src/zonos2_generate.cpp:203-279) for a batch: between zonos2cu_gen_begin and
+ * zonos2cu_gen_end, every zonos2cu_ctx_sample / zonos2cu_ctx_step (and their
+ * host variants) also keeps the step's frame on the device, on the step's
+ * stream: codes clamped to vocab - 1 (:214, :264), the stream ended after the
+ * first frame holding eoa_id (:218-224, :269-276; that frame is kept), at most
+ * max_frames frames per stream, and the next step's input frame (the codes,
+ * then text_pad_id; :238-243).  With the reference's constants (1024 sampled
+ * tokens, eoa_id 1024) no frame can hold eoa_id, so streams run to max_frames,
+ * as in the reference.  gen_begin clears the state; before the first frame the
+ * next input frame is audio_pad_id codes and text_pad_id. */
+int zonos2cu_gen_begin(zonos2cu_ctx *ctx, int max_frames, int eoa_id, int audio_pad_id,
+                       int text_pad_id);
+int zonos2cu_gen_end(zonos2cu_ctx *ctx);
+/* Frames [n_streams][max_frames][n_cb] (entries past a stream's count are -1),
+ * frame counts [n_streams], end-of-audio frame [n_streams] (-1: none); any
+ * pointer may be NULL.  Synchronises the device. */
+int zonos2cu_gen_read(zonos2cu_ctx *ctx, int32_t *frames_host, int32_t *n_frames_host,
+                      int32_t *eos_at_host);
+/* Device pointer to the next step's input frames [n_streams][n_cb + 1] (NULL
+ * before gen_begin). */
+const int32_t *zonos2cu_gen_next_input(zonos2cu_ctx *ctx);
+/* shear_up of every stream's frames (scripts/dac_decode.py:23-30): out_dev
+ * [n_streams][max_frames][n_cb], out[s][t][j] = frames[s][t + j][j] while
+ * t + j < the stream's frame count, audio_pad_id elsewhere. */
+int zonos2cu_gen_shear_up(zonos2cu_ctx *ctx, int32_t *out_dev, void *stream);
+/* The model's input embedding tables, f32 row-major: codebook tables
+ * [n_cb][audio_vocab][dim] (Zonos2Weights::codebook_embeds) and the text table
+ * [text_vocab + 1][dim] (text_embed, padding row last). */
+int zonos2cu_set_embeddings(zonos2cu_ctx *ctx, const float *codebook_tables_host,
+                            const float *text_table_host, int audio_vocab, int text_vocab);
+/* embedding_sum (src/zonos2_model.cpp:116-151) of the next input frames into
+ * out_dev [n_streams][dim] f32: the next model step's input. */
+int zonos2cu_gen_embed_next(zonos2cu_ctx *ctx, float *out_dev, void *stream);
+/* The same on caller buffers: ids_dev [n_frames][n_cb + 1], out_dev [n_frames][dim]. */
+int zonos2cu_embed_frames(const float *codebook_tables_dev, const float *text_table_dev,
+                          int n_cb, int audio_vocab, int text_vocab, int dim,
+                          const int32_t *ids_dev, int n_frames, float *out_dev, void *stream);
+/* Writes frames_host [n_frames][n_cb] in the reference's codes.bin format
+ * (decode_dac_to_wav, src/zonos2_generate.cpp:285-306): int32 n_frames, int32
+ * n_cb, then the codes frame by frame. */
+int zonos2cu_write_codes_bin(const char *path, const int32_t *frames_host, int n_frames,
+                             int n_cb);
+
 /* Reads and clears the device-side error word that bounded waits set when
  * they expire (synchronises the current device).  0 = no error. */
 int zonos2cu_device_error(void);

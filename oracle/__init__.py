@@ -103,6 +103,9 @@ class Oracle:
                                        C.c_int, C.c_float, C.c_void_p, C.c_int]
         L.orc_out_norm.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_float, C.c_void_p]
         L.orc_cfg_blend.argtypes = [C.c_void_p, C.c_void_p, C.c_long, C.c_float, C.c_void_p]
+        L.orc_embed_frames.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
+                                       C.c_void_p, C.c_int, C.c_void_p]
+        L.orc_shear_up.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int32, C.c_void_p]
 
     # generator -------------------------------------------------------------
     def rng_seed(self, seed: int) -> np.ndarray:
@@ -171,6 +174,23 @@ class Oracle:
         self.L.orc_out_norm(_p(x), x.shape[-1], x.size // x.shape[-1], eps, _p(w))
         return x
 
+    def embed_frames(self, cb_tables, text_table, ids):
+        """embedding_sum of frames ids [n][n_cb+1]; tables f32 row-major."""
+        cb_tables = np.ascontiguousarray(cb_tables, np.float32)
+        text_table = np.ascontiguousarray(text_table, np.float32)
+        ids = np.ascontiguousarray(ids, np.int32)
+        n_cb, audio_vocab, dim = cb_tables.shape
+        out = np.zeros((ids.shape[0], dim), np.float32)
+        self.L.orc_embed_frames(_p(cb_tables), _p(text_table), n_cb, audio_vocab,
+                                text_table.shape[0] - 1, dim, _p(ids), ids.shape[0], _p(out))
+        return out
+
+    def shear_up(self, codes, pad=1025):
+        codes = np.ascontiguousarray(codes, np.int32)
+        out = np.empty_like(codes)
+        self.L.orc_shear_up(_p(codes), codes.shape[0], codes.shape[1], pad, _p(out))
+        return out
+
     def cfg_blend(self, cond, uncond, scale):
         cond = np.ascontiguousarray(cond, np.float32)
         uncond = np.ascontiguousarray(uncond, np.float32)
@@ -202,6 +222,10 @@ class Reference:
         L.ref_head_softcap.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p,
                                        C.c_int, C.c_float, C.c_void_p, C.c_int]
         L.ref_out_norm.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_float, C.c_void_p]
+        L.ref_write_codes.argtypes = [C.c_char_p, C.c_void_p, C.c_int, C.c_int]
+        L.ref_write_codes.restype = C.c_int
+        L.ref_embed_frames.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
+                                       C.c_void_p, C.c_int, C.c_void_p]
         L.ref_step.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_long, C.c_float, C.c_int,
                                C.c_float, C.c_float, C.c_float, C.c_int, C.POINTER(C.c_uint64),
                                C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_int,
@@ -234,6 +258,21 @@ class Reference:
                                 nthreads)
         return out
 
+    def write_codes(self, stem, frames):
+        """The reference writes `stem`.codes.bin (and prints a line)."""
+        fr = np.ascontiguousarray(frames, np.int32)
+        return self.L.ref_write_codes(stem.encode(), _p(fr), fr.shape[0], fr.shape[1])
+
+    def embed_frames(self, cb_tables, text_table, ids):
+        cb_tables = np.ascontiguousarray(cb_tables, np.float32)
+        text_table = np.ascontiguousarray(text_table, np.float32)
+        ids = np.ascontiguousarray(ids, np.int32)
+        n_cb, audio_vocab, dim = cb_tables.shape
+        out = np.zeros((ids.shape[0], dim), np.float32)
+        self.L.ref_embed_frames(_p(cb_tables), _p(text_table), n_cb, audio_vocab,
+                                text_table.shape[0] - 1, dim, _p(ids), ids.shape[0], _p(out))
+        return out
+
     def out_norm(self, x, eps=1e-5, weight=None):
         x = np.array(x, np.float32, copy=True, order="C")
         w = None if weight is None else np.ascontiguousarray(weight, np.float32)
@@ -259,3 +298,21 @@ class Reference:
 
     def num_threads(self) -> int:
         return int(self.L.ref_num_threads())
+
+
+def gen_append(codes, frames, n_frames, eos_at, max_frames, codebook_size=1024, eoa_id=1024):
+    """One generation step for a batch, as the reference's loop does it for one
+    stream (src/zonos2_generate.cpp:214-226, :259-276): each sampled code is
+    clamped to codebook_size - 1, a stream that has ended (an EOA code in its
+    previous frame, or max_frames frames) takes no more frames, and a frame
+    holding eoa_id ends its stream after being kept.  codes [S][n_cb];
+    frames [S][max_frames][n_cb], n_frames [S], eos_at [S] are updated in place."""
+    S = codes.shape[0]
+    for s in range(S):
+        if eos_at[s] >= 0 or n_frames[s] >= max_frames:
+            continue
+        f = [min(int(t), codebook_size - 1) for t in codes[s]]
+        frames[s, n_frames[s]] = f
+        if any(t == eoa_id for t in f):
+            eos_at[s] = n_frames[s]
+        n_frames[s] += 1

@@ -76,6 +76,33 @@ void ref_out_norm(float *x, int dim, int n_rows, float eps, const float *weight)
     rms_norm_per_token(x, dim, n_rows, eps, weight);
 }
 
+/* The reference's own embedding_sum on tables given as plain arrays
+ * (cb_tables [n_cb][audio_vocab][dim], text_table [text_vocab+1][dim]). */
+void ref_embed_frames(const float *cb_tables, const float *text_table, int n_cb, int audio_vocab,
+                      int text_vocab, int dim, const int32_t *ids, int n, float *out)
+{
+    Zonos2Weights w;
+    w.cfg.dim = dim;
+    w.cfg.n_codebooks = n_cb;
+    w.cfg.audio_vocab = audio_vocab;
+    w.cfg.text_vocab = text_vocab;
+    for (int cb = 0; cb < n_cb; cb++)
+        w.codebook_embeds[cb].weight.data.assign(cb_tables + (size_t)cb * audio_vocab * dim,
+                                                 cb_tables + (size_t)(cb + 1) * audio_vocab * dim);
+    w.text_embed.weight.data.assign(text_table, text_table + (size_t)(text_vocab + 1) * dim);
+    embedding_sum(w, w.cfg, ids, n, n_cb + 1, out);
+}
+
+/* The reference's own codes.bin writer (decode_dac_to_wav writes
+ * `stem`.codes.bin); returns 1 on success. */
+int ref_write_codes(const char *stem, const int32_t *frames, int n_frames, int n_cb)
+{
+    std::vector<std::vector<int32_t>> codes((size_t)n_frames);
+    for (int t = 0; t < n_frames; t++)
+        codes[t].assign(frames + (size_t)t * n_cb, frames + (size_t)(t + 1) * n_cb);
+    return decode_dac_to_wav(codes, std::string(stem)) ? 1 : 0;
+}
+
 /* W: [n_cb*rows_per_cb, dim]; out: [batch][n_cb][vocab] (the sampled rows). */
 void ref_head_softcap(const float *W, int rows_per_cb, int n_cb, int vocab, int dim,
                       const float *h, int batch, float softcap, float *out, int nthreads)

@@ -311,3 +311,45 @@ void orc_cfg_blend(const float *cond, const float *uncond, long n, float scale, 
 {
     for (long i = 0; i < n; i++) out[i] = uncond[i] + scale * (cond[i] - uncond[i]);
 }
+
+
+/* embedding_sum (src/zonos2_model.cpp:116-151): the input embedding of each
+ * frame, out[t] = sum over codebooks cb (in order) of cb_tables[cb][id_cb]
+ * (ids outside [0, audio_vocab) add nothing), then the text column: a text
+ * token (< text_vocab) adds 5 x its row, the padding id (== text_vocab) adds its
+ * row once, anything else nothing.  Tables are row-major [rows][dim]. */
+void orc_embed_frames(const float *cb_tables, const float *text_table, int n_cb, int audio_vocab,
+                      int text_vocab, int dim, const int32_t *ids, int n, float *out)
+{
+    const int fw = n_cb + 1;
+    for (int t = 0; t < n; t++) {
+        float *o = out + (size_t)t * (size_t)dim;
+        for (int d = 0; d < dim; d++) o[d] = 0.0f;
+        for (int cb = 0; cb < n_cb; cb++) {
+            const int tid = ids[(size_t)t * fw + cb];
+            if (tid >= 0 && tid < audio_vocab) {
+                const float *row = cb_tables + ((size_t)cb * audio_vocab + tid) * (size_t)dim;
+                for (int d = 0; d < dim; d++) o[d] += row[d];
+            }
+        }
+        const int tid = ids[(size_t)t * fw + n_cb];
+        if (tid >= 0 && tid < text_vocab) {
+            const float *row = text_table + (size_t)tid * (size_t)dim;
+            for (int d = 0; d < dim; d++) o[d] += row[d] * 5.0f;
+        } else if (tid == text_vocab) {
+            const float *row = text_table + (size_t)tid * (size_t)dim;
+            for (int d = 0; d < dim; d++) o[d] += row[d];
+        }
+    }
+}
+
+/* shear_up (scripts/dac_decode.py:23-30): undo the delay pattern of n_frames
+ * frames of n_cb codes, out[t][j] = codes[t + j][j] while t + j < n_frames,
+ * pad elsewhere. */
+void orc_shear_up(const int32_t *codes, int n_frames, int n_cb, int32_t pad, int32_t *out)
+{
+    for (int t = 0; t < n_frames; t++)
+        for (int j = 0; j < n_cb; j++)
+            out[(size_t)t * n_cb + j] =
+                t + j < n_frames ? codes[(size_t)(t + j) * n_cb + j] : pad;
+}

@@ -92,6 +92,14 @@ void orc_out_norm(float *x, int dim, int n_rows, float eps, const float *weight)
  * (src/zonos2_generate.cpp:178-183). */
 void orc_cfg_blend(const float *cond, const float *uncond, long n, float scale, float *out);
 
+/* embedding_sum (src/zonos2_model.cpp:116-151) of n frames ids [n][n_cb+1]:
+ * cb_tables [n_cb][audio_vocab][dim], text_table [text_vocab+1][dim], out [n][dim]. */
+void orc_embed_frames(const float *cb_tables, const float *text_table, int n_cb, int audio_vocab,
+                      int text_vocab, int dim, const int32_t *ids, int n, float *out);
+
+/* shear_up (scripts/dac_decode.py:23-30) of codes [n_frames][n_cb]. */
+void orc_shear_up(const int32_t *codes, int n_frames, int n_cb, int32_t pad, int32_t *out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -12,6 +12,7 @@
 
 #include "common.cuh"
 #include "head.cuh"
+#include "generate.cuh"
 #include "sampler.cuh"
 #include "zonos2_cuda.h"
 
@@ -253,6 +254,34 @@ int zonos2cu_head_softcap(const void *W_dev, zonos2cu_dtype dtype, int rows_per_
                        logits_dev, stream, false, 1.0f);
 }
 
+int zonos2cu_embed_frames(const float *codebook_tables_dev, const float *text_table_dev,
+                          int n_cb, int audio_vocab, int text_vocab, int dim,
+                          const int32_t *ids_dev, int n_frames, float *out_dev, void *stream)
+{
+    if (n_cb < 1 || audio_vocab < 1 || text_vocab < 0 || dim < 1 || n_frames < 0)
+        return ZONOS2CU_EINVAL;
+    if (n_frames > 0 && (!codebook_tables_dev || !text_table_dev || !ids_dev || !out_dev))
+        return ZONOS2CU_EINVAL;
+    Z2_CK(z2::launch_embed_frames(codebook_tables_dev, text_table_dev, n_cb, audio_vocab,
+                                  text_vocab, dim, ids_dev, n_frames, out_dev,
+                                  (cudaStream_t)stream));
+    return ZONOS2CU_OK;
+}
+
+int zonos2cu_write_codes_bin(const char *path, const int32_t *frames_host, int n_frames, int n_cb)
+{
+    if (!path || n_frames < 0 || n_cb < 0 || (n_frames > 0 && n_cb > 0 && !frames_host))
+        return ZONOS2CU_EINVAL;
+    FILE *f = fopen(path, "wb");
+    if (!f) return ZONOS2CU_EINVAL;
+    const size_t n = (size_t)n_frames * (size_t)n_cb;
+    const bool ok = fwrite(&n_frames, sizeof(int), 1, f) == 1 &&
+                    fwrite(&n_cb, sizeof(int), 1, f) == 1 &&
+                    (n == 0 || fwrite(frames_host, sizeof(int32_t), n, f) == n);
+    if (fclose(f) != 0 || !ok) return ZONOS2CU_EINVAL;
+    return ZONOS2CU_OK;
+}
+
 int zonos2cu_device_error(void)
 {
     Z2_CK(cudaDeviceSynchronize());
@@ -290,6 +319,17 @@ struct zonos2cu_ctx {
     // classifier-free guidance (zonos2cu_set_cfg): steps take 2S hidden rows
     bool cfg_on = false;
     float cfg_scale = 1.0f;
+    // generation loop state (zonos2cu_gen_begin)
+    bool gen_on = false;
+    int gen_max_frames = 0, gen_eoa = 1024, gen_pad = 1025, gen_text_pad = 519;
+    size_t gen_cap = 0;               // frame slots allocated per stream x streams
+    int32_t *gen_frames = nullptr;    // [S][max_frames][C]
+    int32_t *gen_count = nullptr;     // [2][S]: frames kept, end-of-audio frame (-1: none)
+    int32_t *gen_next = nullptr;      // [S][C+1]: the next step's input frame
+    // input embedding tables (zonos2cu_set_embeddings), f32 row-major
+    float *emb_cb = nullptr;          // [C][audio_vocab][D]
+    float *emb_text = nullptr;        // [text_vocab+1][D]
+    int emb_audio_vocab = 0, emb_text_vocab = 0;
     // host-path staging, grown on demand
     float *in_logits = nullptr;
     size_t in_logits_bytes = 0;
@@ -407,6 +447,11 @@ int zonos2cu_ctx_destroy(zonos2cu_ctx *c)
     cudaFree(c->logits);
     cudaFree(c->norm_w);
     cudaFree(c->normed);
+    cudaFree(c->gen_frames);
+    cudaFree(c->gen_count);
+    cudaFree(c->gen_next);
+    cudaFree(c->emb_cb);
+    cudaFree(c->emb_text);
     cudaFree(c->in_logits);
     cudaFree(c->in_hidden);
     cudaFree(c->out);
@@ -560,6 +605,126 @@ int zonos2cu_set_cfg(zonos2cu_ctx *c, int enable, float scale)
     return ZONOS2CU_OK;
 }
 
+int zonos2cu_gen_begin(zonos2cu_ctx *c, int max_frames, int eoa_id, int audio_pad_id,
+                       int text_pad_id)
+{
+    if (!c || max_frames < 1) return ZONOS2CU_EINVAL;
+    DeviceGuard g(c->device);
+    Z2_CK(cudaDeviceSynchronize());   // no step may still be using the state
+    const size_t S = (size_t)c->dims.n_streams, Cb = (size_t)c->dims.n_cb;
+    const size_t need = S * (size_t)max_frames * Cb;
+    if (need > c->gen_cap) {
+        cudaFree(c->gen_frames);
+        c->gen_frames = nullptr;
+        c->gen_cap = 0;
+        if (need) Z2_CK(cudaMalloc(&c->gen_frames, sizeof(int32_t) * need));
+        c->gen_cap = need;
+    }
+    if (!c->gen_count && S) Z2_CK(cudaMalloc(&c->gen_count, sizeof(int32_t) * 2 * S));
+    if (!c->gen_next && S) Z2_CK(cudaMalloc(&c->gen_next, sizeof(int32_t) * S * (Cb + 1)));
+    if (S) {
+        int32_t *h = new (std::nothrow) int32_t[S * (Cb + 1)];
+        if (!h) return ZONOS2CU_ENOMEM;
+        for (size_t s = 0; s < S; s++) {   // before the first frame: padding everywhere
+            for (size_t cb = 0; cb < Cb; cb++) h[s * (Cb + 1) + cb] = audio_pad_id;
+            h[s * (Cb + 1) + Cb] = text_pad_id;
+        }
+        cudaError_t e = cudaMemsetAsync(c->gen_count, 0, sizeof(int32_t) * S, c->stream);
+        if (e == cudaSuccess)
+            e = cudaMemsetAsync(c->gen_count + S, 0xff, sizeof(int32_t) * S, c->stream);
+        if (e == cudaSuccess)
+            e = cudaMemsetAsync(c->gen_frames, 0xff, sizeof(int32_t) * need, c->stream);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(c->gen_next, h, sizeof(int32_t) * S * (Cb + 1),
+                                cudaMemcpyHostToDevice, c->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+        delete[] h;
+        if (e != cudaSuccess) return cuda_fail(e, "generation state");
+    }
+    c->gen_max_frames = max_frames;
+    c->gen_eoa = eoa_id;
+    c->gen_pad = audio_pad_id;
+    c->gen_text_pad = text_pad_id;
+    c->gen_on = true;
+    return ZONOS2CU_OK;
+}
+
+int zonos2cu_gen_end(zonos2cu_ctx *c)
+{
+    if (!c) return ZONOS2CU_EINVAL;
+    DeviceGuard g(c->device);
+    Z2_CK(cudaDeviceSynchronize());
+    c->gen_on = false;
+    return ZONOS2CU_OK;
+}
+
+int zonos2cu_gen_read(zonos2cu_ctx *c, int32_t *frames_host, int32_t *n_frames_host,
+                      int32_t *eos_at_host)
+{
+    if (!c || !c->gen_count) return ZONOS2CU_ESTATE;
+    DeviceGuard g(c->device);
+    Z2_CK(cudaDeviceSynchronize());
+    const size_t S = (size_t)c->dims.n_streams;
+    if (frames_host && S)
+        Z2_CK(cudaMemcpy(frames_host, c->gen_frames,
+                         sizeof(int32_t) * S * (size_t)c->gen_max_frames * c->dims.n_cb,
+                         cudaMemcpyDeviceToHost));
+    if (n_frames_host && S)
+        Z2_CK(cudaMemcpy(n_frames_host, c->gen_count, sizeof(int32_t) * S, cudaMemcpyDeviceToHost));
+    if (eos_at_host && S)
+        Z2_CK(cudaMemcpy(eos_at_host, c->gen_count + S, sizeof(int32_t) * S,
+                         cudaMemcpyDeviceToHost));
+    return ZONOS2CU_OK;
+}
+
+const int32_t *zonos2cu_gen_next_input(zonos2cu_ctx *c) { return c ? c->gen_next : nullptr; }
+
+int zonos2cu_gen_shear_up(zonos2cu_ctx *c, int32_t *out_dev, void *stream)
+{
+    if (!c || !out_dev) return ZONOS2CU_EINVAL;
+    if (!c->gen_count) return ZONOS2CU_ESTATE;
+    DeviceGuard g(c->device);
+    Z2_CK(z2::launch_shear_up(c->gen_frames, c->gen_count, c->dims.n_streams, c->gen_max_frames,
+                              c->dims.n_cb, c->gen_pad, out_dev, (cudaStream_t)stream));
+    return ZONOS2CU_OK;
+}
+
+int zonos2cu_set_embeddings(zonos2cu_ctx *c, const float *codebook_tables_host,
+                            const float *text_table_host, int audio_vocab, int text_vocab)
+{
+    if (!c || !codebook_tables_host || !text_table_host || c->dims.dim < 1 || audio_vocab < 1 ||
+        text_vocab < 0)
+        return ZONOS2CU_EINVAL;
+    DeviceGuard g(c->device);
+    Z2_CK(cudaDeviceSynchronize());
+    const size_t D = (size_t)c->dims.dim, Cb = (size_t)c->dims.n_cb;
+    const size_t nb = sizeof(float) * Cb * (size_t)audio_vocab * D;
+    const size_t tb = sizeof(float) * ((size_t)text_vocab + 1) * D;
+    cudaFree(c->emb_cb);
+    cudaFree(c->emb_text);
+    c->emb_cb = nullptr;
+    c->emb_text = nullptr;
+    Z2_CK(cudaMalloc(&c->emb_cb, nb));
+    Z2_CK(cudaMalloc(&c->emb_text, tb));
+    Z2_CK(cudaMemcpyAsync(c->emb_cb, codebook_tables_host, nb, cudaMemcpyHostToDevice, c->stream));
+    Z2_CK(cudaMemcpyAsync(c->emb_text, text_table_host, tb, cudaMemcpyHostToDevice, c->stream));
+    Z2_CK(cudaStreamSynchronize(c->stream));
+    c->emb_audio_vocab = audio_vocab;
+    c->emb_text_vocab = text_vocab;
+    return ZONOS2CU_OK;
+}
+
+int zonos2cu_gen_embed_next(zonos2cu_ctx *c, float *out_dev, void *stream)
+{
+    if (!c || !out_dev) return ZONOS2CU_EINVAL;
+    if (!c->gen_next || !c->emb_cb) return ZONOS2CU_ESTATE;
+    DeviceGuard g(c->device);
+    Z2_CK(z2::launch_embed_frames(c->emb_cb, c->emb_text, c->dims.n_cb, c->emb_audio_vocab,
+                                  c->emb_text_vocab, c->dims.dim, c->gen_next, c->dims.n_streams,
+                                  out_dev, (cudaStream_t)stream));
+    return ZONOS2CU_OK;
+}
+
 int zonos2cu_ctx_sample(zonos2cu_ctx *c, const float *logits_dev, long long row_stride,
                         const zonos2cu_sample_params *params, int delay_step, int32_t *codes_dev,
                         int32_t *flags_dev, void *stream)
@@ -576,6 +741,11 @@ int zonos2cu_ctx_sample(zonos2cu_ctx *c, const float *logits_dev, long long row_
                      delay_step, codes_dev, flags_dev, (cudaStream_t)stream, c->counts,
                      c->presence, /*allow_lane_major*/ true);
     if (rc) return rc;
+    if (c->gen_on)   // the generation loop keeps this step's frame
+        Z2_CK(z2::launch_gen_append(codes_dev, d.n_streams, d.n_cb, d.vocab, c->gen_eoa,
+                                    c->gen_text_pad, c->gen_max_frames, c->gen_frames,
+                                    c->gen_count, c->gen_count + d.n_streams, c->gen_next,
+                                    (cudaStream_t)stream));
     if (d.hist_len > 0) c->hist_pos = (c->hist_pos + 1) % d.hist_len;
     return ZONOS2CU_OK;
 }

@@ -38,6 +38,9 @@ EXPORTS = (
     "zonos2cu_ctx_sample", "zonos2cu_ctx_sample_host", "zonos2cu_ctx_step",
     "zonos2cu_ctx_step_host", "zonos2cu_ctx_stream", "zonos2cu_device_error",
     "zonos2cu_step_noalloc", "zonos2cu_set_out_norm", "zonos2cu_set_cfg",
+    "zonos2cu_gen_begin", "zonos2cu_gen_end", "zonos2cu_gen_read", "zonos2cu_gen_next_input",
+    "zonos2cu_gen_shear_up", "zonos2cu_set_embeddings", "zonos2cu_gen_embed_next",
+    "zonos2cu_embed_frames", "zonos2cu_write_codes_bin",
 )
 
 
@@ -98,6 +101,15 @@ def lib() -> C.CDLL:
         "zonos2cu_set_rng": (i, [vp, vp]),
         "zonos2cu_set_out_norm": (i, [vp, i, vp, f]),
         "zonos2cu_set_cfg": (i, [vp, i, f]),
+        "zonos2cu_gen_begin": (i, [vp, i, i, i, i]),
+        "zonos2cu_gen_end": (i, [vp]),
+        "zonos2cu_gen_read": (i, [vp, vp, vp, vp]),
+        "zonos2cu_gen_next_input": (vp, [vp]),
+        "zonos2cu_gen_shear_up": (i, [vp, vp, vp]),
+        "zonos2cu_set_embeddings": (i, [vp, vp, vp, i, i]),
+        "zonos2cu_gen_embed_next": (i, [vp, vp, vp]),
+        "zonos2cu_embed_frames": (i, [vp, vp, i, i, i, i, vp, i, vp, vp]),
+        "zonos2cu_write_codes_bin": (i, [C.c_char_p, vp, i, i]),
         "zonos2cu_get_rng": (i, [vp, vp]),
         "zonos2cu_set_allow": (i, [vp, vp]),
         "zonos2cu_ctx_sample": (i, [vp, vp, ll, C.POINTER(SampleParams), i, vp, vp, vp]),
@@ -294,6 +306,42 @@ class Context:
         """Guidance blend; steps then take 2 * n_streams hidden rows (2s cond, 2s+1 uncond)."""
         _check(lib().zonos2cu_set_cfg(self.h, int(enable), C.c_float(scale)), "set_cfg")
 
+    # ---- generation loop
+    def gen_begin(self, max_frames: int, eoa_id: int = 1024, audio_pad_id: int = 1025,
+                  text_pad_id: int = 519) -> None:
+        _check(lib().zonos2cu_gen_begin(self.h, max_frames, eoa_id, audio_pad_id, text_pad_id),
+               "gen_begin")
+        self._max_frames = max_frames
+
+    def gen_end(self) -> None:
+        _check(lib().zonos2cu_gen_end(self.h), "gen_end")
+
+    def gen_read(self):
+        """(frames [S][max_frames][n_cb], n_frames [S], eos_at [S]) as numpy arrays."""
+        s = self.shape
+        frames = np.zeros((s.n_streams, self._max_frames, s.n_cb), np.int32)
+        nf = np.zeros(s.n_streams, np.int32)
+        eos = np.zeros(s.n_streams, np.int32)
+        _check(lib().zonos2cu_gen_read(self.h, frames.ctypes.data, nf.ctypes.data,
+                                       eos.ctypes.data), "gen_read")
+        return frames, nf, eos
+
+    def gen_next_input_ptr(self) -> int:
+        return lib().zonos2cu_gen_next_input(self.h) or 0
+
+    def gen_shear_up(self, out, stream=None) -> None:
+        _check(lib().zonos2cu_gen_shear_up(self.h, _ptr(out), _stream(stream)), "gen_shear_up")
+
+    def set_embeddings(self, codebook_tables, text_table) -> None:
+        cb = np.ascontiguousarray(codebook_tables, np.float32)
+        tx = np.ascontiguousarray(text_table, np.float32)
+        _check(lib().zonos2cu_set_embeddings(self.h, cb.ctypes.data, tx.ctypes.data, cb.shape[1],
+                                             tx.shape[0] - 1), "set_embeddings")
+
+    def gen_embed_next(self, out, stream=None) -> None:
+        _check(lib().zonos2cu_gen_embed_next(self.h, _ptr(out), _stream(stream)),
+               "gen_embed_next")
+
     def sample(self, logits, params: SampleParams, codes, flags=None, delay_step=-1,
                row_stride=None, stream=None) -> None:
         """Device step on ``stream`` (default: torch's current stream)."""
@@ -320,3 +368,19 @@ class Context:
         rc = lib().zonos2cu_ctx_step_host(self.h, _ptr(hidden), dtype, C.byref(params),
                                           delay_step, _ptr(codes), _ptr(flags))
         _check(rc, "zonos2cu_ctx_step_host")
+
+
+def embed_frames(codebook_tables, text_table, ids, out, stream=None) -> None:
+    """embedding_sum on device buffers: tables [n_cb][audio_vocab][dim] and
+    [text_vocab+1][dim] f32, ids [n][n_cb+1] int32, out [n][dim] f32."""
+    n_cb, audio_vocab, dim = codebook_tables.shape
+    _check(lib().zonos2cu_embed_frames(_ptr(codebook_tables), _ptr(text_table), n_cb, audio_vocab,
+                                       text_table.shape[0] - 1, dim, _ptr(ids), ids.shape[0],
+                                       _ptr(out), _stream(stream)), "zonos2cu_embed_frames")
+
+
+def write_codes_bin(path: str, frames) -> None:
+    """frames [n_frames][n_cb] int32 -> the reference's codes.bin format."""
+    fr = np.ascontiguousarray(frames, np.int32)
+    _check(lib().zonos2cu_write_codes_bin(path.encode(), fr.ctypes.data if fr.size else None,
+                                          fr.shape[0], fr.shape[1]), "zonos2cu_write_codes_bin")
