@@ -159,18 +159,11 @@ __device__ __forceinline__ float prologue(float x, int i, uint32_t seenm, uint32
     return (fin && ((allowm >> i) & 1u)) ? __fmul_rn(x, f) : -INFINITY;
 }
 
-// Gap bucket of a logit, round((max - v) / width) clamped to 126 (the
-// open-ended last bucket), in the low byte of the result; monotone
-// non-increasing in v.  -inf lands in 126.
-__device__ __forceinline__ uint32_t bucket_bits(float v, float sc, float Msc)
-{
-    const float t = fminf(__fmaf_rn(-v, sc, Msc), (float)(kBuckets - 2));
-    return __float_as_uint(__fadd_rn(t, 0x1p23f));
-}
-
-// The bucket coordinate of bucket_bits, (max - v) / width + 1/2 in [0, 126.5],
-// rounded to a multiple of 2^-15: an integer below 2^22, monotone
-// non-increasing in v.
+// Gap bucket of a logit: t = min(fma(-v, 1/width, max/width), 126), and the
+// bucket is round(t), read from the low byte of t + 2^23 (the histogram does
+// this two slots at a time); -inf lands in 126, the open-ended last bucket.
+// gap_q15 is the same coordinate t + 1/2 in [0, 126.5] rounded to a multiple of
+// 2^-15: an integer below 2^22, monotone non-increasing in v.
 __device__ __forceinline__ uint32_t gap_q15(float v, float sc, float Msc)
 {
     const float t = fminf(__fmaf_rn(-v, sc, Msc), (float)(kBuckets - 2));
@@ -883,17 +876,23 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
         bool nonfin = false;
         {
             float acc = 1.0f;
-            if (a.rho >= 1.0f) {
-                acc = 0.0f;
+            if (a.rho >= 1.0f) {   // slots in pairs: the products and the fma packed (f32x2)
+                float2 acc2 = make_float2(0.0f, 0.0f);
+                const float2 ir2 = make_float2(a.inv_rho, a.inv_rho);
+                const float2 r2 = make_float2(a.rho, a.rho);
+                const float2 zero2 = make_float2(0.0f, 0.0f);
 #pragma unroll
-                for (int i = 0; i < 32; i++) {
-                    const float x = v[i];
-                    acc = __fmaf_rn(x, 0.0f, acc);
-                    const float pn = fminf(__fmul_rn(x, a.inv_rho), __fmul_rn(x, a.rho));
-                    const float z = ((seenm >> i) & 1u) ? pn : x;
-                    v[i] = ((km >> i) & 1u) ? z : -INFINITY;
-                    mx = fmaxf(mx, v[i]);
+                for (int i = 0; i < 32; i += 2) {
+                    const float2 x = make_float2(v[i], v[i + 1]);
+                    acc2 = __ffma2_rn(x, zero2, acc2);
+                    const float2 pa = __fmul2_rn(x, ir2), pb = __fmul2_rn(x, r2);
+                    const float z0 = ((seenm >> i) & 1u) ? fminf(pa.x, pb.x) : x.x;
+                    const float z1 = ((seenm >> (i + 1)) & 1u) ? fminf(pa.y, pb.y) : x.y;
+                    v[i] = ((km >> i) & 1u) ? z0 : -INFINITY;
+                    v[i + 1] = ((km >> (i + 1)) & 1u) ? z1 : -INFINITY;
+                    mx = fmaxf(mx, fmaxf(v[i], v[i + 1]));
                 }
+                acc = __fadd_rn(acc2.x, acc2.y);
             }
             if (__any_sync(kFull, !(acc == 0.0f)))
                 mx = careful_prologue(rowf, lane, V, seenm, allowm, validm, a.rho, a.inv_rho, v,
@@ -931,17 +930,25 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
             // bucket_bits = 0x4B000000 + b, so (bits * 4 + hbase) mod 2^32 is the
             // shared address of counter b
             const uint32_t hbase = smem_u32(hist) - 0x2C000000u;
+            const float2 nsc2 = make_float2(-sc, -sc), msc2 = make_float2(Msc, Msc);
+            const float2 mag2 = make_float2(0x1p23f, 0x1p23f);
 #pragma unroll
             for (int j = 0; j < 8; j++) {
                 uint32_t bb[4];
 #pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const uint32_t bits = bucket_bits(v[4 * j + e], sc, Msc);
-                    if (bits < 0x4B000000u + (uint32_t)(kBuckets - 2))
-                        asm volatile("red.shared.add.u32 [%0], 1;" ::"r"(bits * 4u + hbase)
-                                     : "memory");
-                    bb[e] = bits;
+                for (int e = 0; e < 4; e += 2) {   // bucket_bits of two slots at once
+                    float2 t = __ffma2_rn(make_float2(v[4 * j + e], v[4 * j + e + 1]), nsc2, msc2);
+                    t.x = fminf(t.x, (float)(kBuckets - 2));
+                    t.y = fminf(t.y, (float)(kBuckets - 2));
+                    t = __fadd2_rn(t, mag2);
+                    bb[e] = __float_as_uint(t.x);
+                    bb[e + 1] = __float_as_uint(t.y);
                 }
+#pragma unroll
+                for (int e = 0; e < 4; e++)
+                    if (bb[e] < 0x4B000000u + (uint32_t)(kBuckets - 2))
+                        asm volatile("red.shared.add.u32 [%0], 1;" ::"r"(bb[e] * 4u + hbase)
+                                     : "memory");
                 bkt[lane + 32 * j] = __byte_perm(__byte_perm(bb[0], bb[1], 0x0040u),
                                                  __byte_perm(bb[2], bb[3], 0x0040u), 0x5410u);
             }
