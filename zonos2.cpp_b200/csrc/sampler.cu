@@ -634,6 +634,31 @@ __device__ __forceinline__ float careful_prologue(const float *rowf, int lane, i
     return mx;
 }
 
+// Odd-even transposition rounds (descending) on 128 keys held four per lane
+// (element 4*l + e) until a round swaps nothing; true if sorted within `cap`
+// rounds.
+__device__ __forceinline__ bool oets_desc(uint32_t k[4], int lane, int cap)
+{
+    for (int round = 0; round < cap; round++) {
+        uint32_t moved = 0u;
+        // pairs (0,1) (2,3)
+        moved |= (uint32_t)(k[0] < k[1]) | (uint32_t)(k[2] < k[3]);
+        const uint32_t a0 = max(k[0], k[1]), a1 = min(k[0], k[1]);
+        const uint32_t a2 = max(k[2], k[3]), a3 = min(k[2], k[3]);
+        // pairs (1,2) and (3, next lane's 0)
+        moved |= (uint32_t)(a1 < a2);
+        k[1] = max(a1, a2);
+        k[2] = min(a1, a2);
+        const uint32_t nx = __shfl_down_sync(kFull, a0, 1);   // the next lane's first
+        const uint32_t pv = __shfl_up_sync(kFull, a3, 1);     // the previous lane's last
+        moved |= (uint32_t)(lane < 31 && a3 < nx);
+        k[3] = lane < 31 ? max(a3, nx) : a3;
+        k[0] = lane > 0 ? min(a0, pv) : a0;
+        if (!__any_sync(kFull, moved != 0u)) return true;
+    }
+    return false;
+}
+
 // Out of line: the exact-key sort for the rare rows whose quantized order fails.
 __device__ __noinline__ void sort_keys_exact(uint64_t key[4], int lane);
 
@@ -996,6 +1021,11 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
 #pragma unroll
             for (int j = 0; j < 8; j++) selm |= bytes_le(bkt[lane + 32 * j], bc4) << (4 * j);
             selm &= km;
+            {   // counters -> each bucket's first position in bucket order
+                const int c0 = incl - tot;
+                reinterpret_cast<uint4 *>(hist)[lane] =
+                    make_uint4(c0, c0 + h[0], c0 + h[0] + h[1], c0 + h[0] + h[1] + h[2]);
+            }
 
             // the uniform: its producer has finished once waited for
             if (!drawn) {
@@ -1019,19 +1049,19 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
                 __syncwarp();
                 if (cb_nx < NCB) issue(s_nx, cb_nx);
             } else {
-                // ---- 5. candidates -> four per lane, as 32-bit sort keys (compaction
-                // through shared memory).  p is a non-increasing function of the gap,
-                // so the keys order the candidates by the gap's bucket coordinate
-                // (max - l) / width, monotone in l like the bucket and kept to 15
-                // fractional bits, then by token.  That is the exact (p desc, token asc)
-                // order unless two gaps share a quantum or two gaps give one p; the
-                // order of the exact keys is checked below and, if broken, sorted
-                // outright.
+                // ---- 5. candidates -> four per lane, as 32-bit sort keys, scattered in
+                // bucket order (the histogram's prefix gives each bucket's first slot).
+                // p is a non-increasing function of the gap, so the keys order the
+                // candidates by the gap's bucket coordinate (max - l) / width, monotone
+                // in l like the bucket and kept to 15 fractional bits, then by token.
+                // That is the exact (p desc, token asc) order unless two gaps share a
+                // quantum or two gaps give one p; the order of the exact keys is
+                // checked below and, if broken, sorted outright.
                 uint32_t *stage = reinterpret_cast<uint32_t *>(region + kStageOffset);
-                {   // as many rounds as the fullest lane needs, without branches: a lane
-                    // with nothing left writes a spare entry past the stage
+                __syncwarp();   // bucket offsets in place
+                {   // as many rounds as the fullest lane needs: a lane with nothing left
+                    // writes a spare entry past the stage
                     const int cnt = __popc(selm);
-                    int pos = warp_incl_scan(cnt, lane) - cnt;
                     const int rounds = __reduce_max_sync(kFull, (unsigned)cnt);
                     uint32_t sm = selm;
                     for (int k = 0; k < rounds; k++) {
@@ -1039,9 +1069,10 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
                         const int i = __ffs(sm | 0x80000000u) - 1;
                         sm &= sm - 1u;
                         const int t = slot_token(lane, i);
-                        stage[has ? pos : kRegSortMax] =
-                            ~((gap_q15(rowf[t], sc, Msc) << 10) | (uint32_t)t);
-                        pos += has;
+                        const uint32_t b8 = (bkt[lane + 32 * (i >> 2)] >> (8 * (i & 3))) & 0xffu;
+                        int pos = kRegSortMax;
+                        if (has) pos = (int)atomicAdd(hist + b8, 1u);
+                        stage[pos] = ~((gap_q15(rowf[t], sc, Msc) << 10) | (uint32_t)t);
                     }
                 }
                 __syncwarp();
@@ -1053,7 +1084,10 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
                     ck[2] = 4 * lane + 2 < n_c ? k4.z : 0u;
                     ck[3] = 4 * lane + 3 < n_c ? k4.w : 0u;
                 }
-                bitonic128_desc(ck, lane);
+                // Bucket order leaves the keys unsorted only inside buckets of a few
+                // candidates: odd-even transposition rounds finish them; a bitonic
+                // network takes over if 16 rounds do not.
+                if (!oets_desc(ck, lane, 16)) bitonic128_desc(ck, lane);
                 const SmemExpTable tab{exptab};
                 uint64_t key[4];
                 int np = 0;
