@@ -728,6 +728,19 @@ __device__ __forceinline__ int first_flagged(uint32_t f4)
 // margin (taken 2.5x) equal the reference's; the rest are made term by term.
 constexpr double kSumEta = 640.0 * 0x1p-24;
 
+// min-p keeps position i while fl(p_i / S) >= fl(fl(p_0 / S) * min_p); the sum S
+// cancels, so p_i >= p_0 * min_p * (1 + 2^-24) keeps it and
+// p_i < p_0 * min_p * (1 - 3 * 2^-24) drops it; the margin is taken 5x.
+constexpr double kMinpEta = 16.0 * 0x1p-24;
+
+// The probability at sorted position i, in every lane.
+__device__ __forceinline__ float key_p_at(const uint64_t key[4], int i)
+{
+    const int e = i & 3;
+    const uint64_t k = e == 0 ? key[0] : e == 1 ? key[1] : e == 2 ? key[2] : key[3];
+    return __shfl_sync(kFull, key_p(k), i >> 2);
+}
+
 __device__ __noinline__ void sort_keys_exact(uint64_t key[4], int lane)
 {
     bitonic128_desc(key, lane);
@@ -1123,18 +1136,17 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
 
                 // ---- 7. top-k / top-p / min-p (src/zonos2_generate.cpp:55-84).  The
                 // list is keys[0..m) (positive probabilities, sorted) followed by
-                // zero-probability tokens in token order, n entries in all; every sum
-                // the reference recomputes from zero over a sorted prefix is one of
-                // the running prefix sums pf.  The top-p cut is found from exact
-                // prefix sums with the error margin above; only its own prefix is then
-                // summed term by term.
+                // zero-probability tokens in token order, n entries in all.  Every
+                // decision is taken from the exact prefix sums P with the error margin
+                // above (min-p needs none of the sums: the reference divides both sides
+                // of its comparison by the same sum); a row where one is too close to
+                // call is redone term by term, with the reference's running f32 sums.
                 const int m = min(n_pos, K);
                 int n = K;
-                float *pf = reinterpret_cast<float *>(region + kPfOffset);
-                float *q = reinterpret_cast<float *>(region + kQOffset);
+                int hit = -1;   // 1 + the walk's position; -1 when it runs past the positives
+                bool fast = true;
                 double P[4];
                 prefix_f64(key, m, lane, P);
-                int cut = -1;   // > 0: top-p certainly cuts after `cut` entries
                 if (a.top_p < 1.0f) {
                     const double tpS = (double)a.top_p * prefix_at(P, m - 1);
                     uint32_t nb = 0u;   // positions not certainly below top_p
@@ -1142,49 +1154,68 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
                     for (int e = 0; e < 4; e++)
                         if (4 * lane + e < m && !(P[e] * (1.0 + kSumEta) < tpS)) nb |= 1u << e;
                     const int jj = first_flagged(nb);
-                    if (jj < 128 && prefix_at(P, jj) * (1.0 - kSumEta) >= tpS) cut = jj + 1;
-                }
-                float S;
-                if (cut > 0) {
-                    n = cut;
-                    if (lane == 0) prefix_sums(ps, pf, n);
-                    __syncwarp();
-                    S = pf[n - 1];
-                } else {   // no certain cut: the reference's sums and walk, term by term
-                    if (lane == 0) prefix_sums(ps, pf, m);
-                    __syncwarp();
-                    S = pf[m - 1];
-                    if (a.top_p < 1.0f) {
-                        const int c = walk_cdf(ps, q, m, S, a.top_p, lane);
-                        if (c > 0) n = c;  // never inside the zero tail: the sum stops growing
-                        S = pf[min(n, m) - 1];
+                    if (jj < 128) {   // 128: the sum never reaches top_p, no cut
+                        if (prefix_at(P, jj) * (1.0 - kSumEta) >= tpS) n = jj + 1;
+                        else fast = false;
                     }
                 }
-                if (a.min_p > 0.0f) {
-                    const float thresh = (ps[0] / S) * a.min_p;
-                    const int mm = min(n, m);
-                    int j = minp_cut(ps, mm, S, thresh, lane);
-                    if (j == mm && n > mm) j = (0.0f >= thresh) ? n : mm;
-                    n = j;
-                    S = pf[min(n, m) - 1];
+                if (fast && a.min_p > 0.0f) {
+                    if (!(a.min_p >= 0x1p-100f)) {   // thresholds near the f32 range's end
+                        fast = false;
+                    } else {   // keep while p_i >= p_0 * min_p
+                        const int mm = min(n, m);
+                        const double thr =
+                            (double)__shfl_sync(kFull, key_p(key[0]), 0) * (double)a.min_p;
+                        uint32_t nk = 0u;   // positions not certainly kept
+#pragma unroll
+                        for (int e = 0; e < 4; e++)
+                            if (4 * lane + e < mm && !((double)key_p(key[e]) >= thr * (1.0 + kMinpEta)))
+                                nk |= 1u << e;
+                        const int jj = first_flagged(nk);
+                        if (jj == 128)
+                            n = mm;   // every positive kept; the zero tail is not (thresh > 0)
+                        else if ((double)key_p_at(key, jj) < thr * (1.0 - kMinpEta))
+                            n = jj;
+                        else
+                            fast = false;
+                    }
                 }
                 // ---- 8. one uniform, CDF walk (src/zonos2_generate.cpp:86-92): the
-                // first position whose partial sum reaches u, by the same margin
-                int hit;   // 1 + that position; -1 when the walk runs past the positives
-                {
+                // first position whose partial sum reaches u
+                if (fast) {
                     const int len = min(n, m);
-                    const double uS = (double)u * (double)S;
+                    const double uS = (double)u * prefix_at(P, len - 1);
                     uint32_t nb = 0u;   // positions not certainly below u
 #pragma unroll
                     for (int e = 0; e < 4; e++)
                         if (4 * lane + e < len && !(uS > P[e] * (1.0 + kSumEta))) nb |= 1u << e;
                     const int jj = first_flagged(nb);
-                    if (jj == 128)
-                        hit = -1;
-                    else if (uS <= prefix_at(P, jj) * (1.0 - kSumEta))
-                        hit = jj + 1;
-                    else
-                        hit = walk_cdf(ps, q, len, S, u, lane);
+                    if (jj < 128) {
+                        if (uS <= prefix_at(P, jj) * (1.0 - kSumEta)) hit = jj + 1;
+                        else fast = false;
+                    }
+                }
+                if (!fast) {   // term by term, as the reference
+                    float *pf = reinterpret_cast<float *>(region + kPfOffset);
+                    float *q = reinterpret_cast<float *>(region + kQOffset);
+                    n = K;
+                    if (lane == 0) prefix_sums(ps, pf, m);
+                    __syncwarp();
+                    float S = pf[m - 1];
+                    if (a.top_p < 1.0f) {
+                        const int c = walk_cdf(ps, q, m, S, a.top_p, lane);
+                        if (c > 0) n = c;  // never inside the zero tail: the sum stops growing
+                        S = pf[min(n, m) - 1];
+                    }
+                    if (a.min_p > 0.0f) {
+                        const float thresh = (ps[0] / S) * a.min_p;
+                        const int mm = min(n, m);
+                        int jn = minp_cut(ps, mm, S, thresh, lane);
+                        if (jn == mm && n > mm) jn = (0.0f >= thresh) ? n : mm;
+                        n = jn;
+                        S = pf[min(n, m) - 1];
+                    }
+                    hit = walk_cdf(ps, q, min(n, m), S, u, lane);
                 }
                 if (lane == 0)
                     tok = pick_token(keys, hit > 0 ? hit - 1 : -1, n, m, n_pos,
