@@ -164,9 +164,10 @@ __device__ __forceinline__ float prologue(float x, int i, uint32_t seenm, uint32
 // this two slots at a time); -inf lands in 126, the open-ended last bucket.
 // gap_q15 is the same coordinate t + 1/2 in [0, 126.5] rounded to a multiple of
 // 2^-15: an integer below 2^22, monotone non-increasing in v.
-__device__ __forceinline__ uint32_t gap_q15(float v, float sc, float Msc)
+__device__ __forceinline__ uint32_t gap_q15(float v, float sc, float Msc, uint32_t *bucket)
 {
     const float t = fminf(__fmaf_rn(-v, sc, Msc), (float)(kBuckets - 2));
+    *bucket = __float_as_uint(__fadd_rn(t, 0x1p23f)) & 0xffu;   // as the histogram's
     return __float_as_uint(__fmaf_rn(t, 32768.0f, 16384.0f + 0x1p23f)) - 0x4B000000u;
 }
 
@@ -961,7 +962,8 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
             // open-ended last bucket holds most of a row: it is not counted, its
             // count follows from the number of kept logits.
             const float bw = fmaxf(T * 0.125f, fabsf(M) * 0x1p-18f + T * 0x1p-14f);
-            const float sc = 1.0f / bw;
+            float sc;   // any positive scale will do: every bucket below is computed from it
+            asm("rcp.approx.f32 %0, %1;" : "=f"(sc) : "f"(bw));
             const float Msc = M * sc;
             reinterpret_cast<uint4 *>(hist)[lane] = make_uint4(0u, 0u, 0u, 0u);
             __syncwarp();
@@ -1082,10 +1084,11 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
                         const int i = __ffs(sm | 0x80000000u) - 1;
                         sm &= sm - 1u;
                         const int t = slot_token(lane, i);
-                        const uint32_t b8 = (bkt[lane + 32 * (i >> 2)] >> (8 * (i & 3))) & 0xffu;
+                        uint32_t b8;
+                        const uint32_t q = gap_q15(rowf[t], sc, Msc, &b8);
                         int pos = kRegSortMax;
                         if (has) pos = (int)atomicAdd(hist + b8, 1u);
-                        stage[pos] = ~((gap_q15(rowf[t], sc, Msc) << 10) | (uint32_t)t);
+                        stage[pos] = ~((q << 10) | (uint32_t)t);
                     }
                 }
                 __syncwarp();
