@@ -61,9 +61,9 @@ ROW_BYTES = 4 * VOCAB + 4 * HIST + 8 + 128 / NCB
 DESIGN_ROW_BYTES = 4 * VOCAB + 128 + 8 + 8 + 8 + 128 / NCB + 64 / NCB
 # DRAM bytes (read + write) of one sample_rows_kernel launch on this workload,
 # from an ncu capture of `bench.py --steps 12 --warmup 3 --no-cpu-baseline
-# --no-head`, launch 11 (dram__bytes_read.sum 170.45 MB +
-# dram__bytes_write.sum 6.11 MB).
-SAMPLER_TRAFFIC_BYTES = 176.56e6
+# --no-head`, launch 11 (dram__bytes_read.sum 167.09 MB +
+# dram__bytes_write.sum 7.23 MB).
+SAMPLER_TRAFFIC_BYTES = 174.32e6
 # Kernels of ours per decode step: the uniform draw and the persistent sampler.
 LAUNCHES_PER_STEP = 2
 
