@@ -102,3 +102,32 @@ def test_out_norm_cfg_bf16(z2, oracle, cuda, S, cfg):
     oc, _, _ = oracle.step(got, prm, oracle.rng_seed_streams(7, S), hist, hist_pos=0, exp_mode=1)
     assert (codes.cpu().numpy() == oc).all()
     ctx.close()
+
+
+def test_host_step_matches_device_step(z2, oracle, cuda):
+    """zonos2cu_ctx_step_host with the norm and guidance on (it copies 2*S hidden
+    rows) samples the same codes as the device call on the same state."""
+    import torch
+    rs = np.random.default_rng(31)
+    S, D = 3, 2048
+    Wb, _ = _bf16(rs.normal(0, 0.02, size=(9 * 1024, D)).astype(np.float32))
+    gamma = rs.normal(1, 0.1, D).astype(np.float32)
+    hb, _ = _bf16(rs.normal(0, 4, (2 * S, D)).astype(np.float32))
+    p = z2.SampleParams(0.8, 50, 0.95, 0.02, 1.0, 1023)
+    out = []
+    for host in (False, True):
+        ctx = z2.Context(0, S, 9, 1024, D, 0, seed=11)
+        ctx.set_head(Wb, z2.BF16, 1024)
+        ctx.set_out_norm(gamma, 1e-5)
+        ctx.set_cfg(1.6)
+        if host:
+            codes = np.zeros((S, 9), np.int32)
+            ctx.step_host(hb, z2.BF16, p, codes)
+        else:
+            c = torch.zeros((S, 9), dtype=torch.int32, device=cuda)
+            ctx.step(_dev(hb, cuda), z2.BF16, p, c)
+            torch.cuda.synchronize()
+            codes = c.cpu().numpy()
+        out.append(codes)
+        ctx.close()
+    assert (out[0] == out[1]).all()
