@@ -712,13 +712,36 @@ __device__ __forceinline__ double prefix_at(const double P[4], int i)
 // Smallest position 4*l + e whose bit e is set in lane l's f4; 128 if none.
 __device__ __forceinline__ int first_flagged(uint32_t f4)
 {
-    int best = 128;
-#pragma unroll
-    for (int e = 0; e < 4; e++) {
-        const uint32_t b = __ballot_sync(kFull, (f4 >> e) & 1u);
-        if (b) best = min(best, 4 * (__ffs(b) - 1) + e);
-    }
-    return best;
+    const uint32_t b = __ballot_sync(kFull, f4 != 0u);
+    if (b == 0u) return 128;
+    const int fl = __ffs(b) - 1;
+    return 4 * fl + __ffs(__shfl_sync(kFull, f4, fl)) - 1;
+}
+
+// max(a, b, c) in one instruction (sm_100); a NaN operand is ignored as by fmaxf.
+__device__ __forceinline__ float fmax3(float a, float b, float c)
+{
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t sel4u(const uint32_t x[4], int e)
+{
+    return e == 0 ? x[0] : e == 1 ? x[1] : e == 2 ? x[2] : x[3];
+}
+__device__ __forceinline__ float sel4f(const float x[4], int e)
+{
+    return e == 0 ? x[0] : e == 1 ? x[1] : e == 2 ? x[2] : x[3];
+}
+
+// 2^a by the hardware approximation (relative error far below 2^-20 for
+// results in the normal range).
+__device__ __forceinline__ float ex2_approx(float a)
+{
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(a));
+    return r;
 }
 
 // A partial sum the reference accumulates term by term in f32 over sorted
@@ -745,6 +768,133 @@ __device__ __forceinline__ float key_p_at(const uint64_t key[4], int i)
 __device__ __noinline__ void sort_keys_exact(uint64_t key[4], int lane)
 {
     bitonic128_desc(key, lane);
+}
+
+// Steps 6-8 in exact arithmetic, for the rows the certified form cannot settle.
+// Lane l holds candidates 4l + e (token t_e, penalized logit l_e) in the
+// quantized order.  Exact probabilities make exact keys (sorted outright if the
+// quantized order breaks theirs); decisions come from exact f64 prefix sums
+// where the reference's margin allows, else term by term with the reference's
+// f32 sums.  The row's logits are no longer in shared memory: the next row's
+// copy may be landing there.  Returns the token in lane 0.
+__device__ __noinline__ int exact_decide(unsigned char *region, const double *exptab, int n_c, int K,
+                                         int V, int pad, float top_p, float min_p, double inv_temp,
+                                         float M, float u, int lane, float l0, float l1, float l2,
+                                         float l3, uint32_t t0, uint32_t t1, uint32_t t2,
+                                         uint32_t t3)
+{
+    const float lv[4] = {l0, l1, l2, l3};
+    const uint32_t tk[4] = {t0, t1, t2, t3};
+    const SmemExpTable tab{exptab};
+    uint64_t key[4];
+    int np = 0;
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        key[e] = 0ull;   // sorts after every candidate
+        if (4 * lane + e < n_c) {
+            const float p = row_prob(lv[e], M, inv_temp, tab);
+            np += p > 0.0f;
+            key[e] = make_key(p, (int)tk[e]);
+        }
+    }
+    const int n_pos = __reduce_add_sync(kFull, np);
+    {
+        const uint64_t nx = __shfl_down_sync(kFull, key[0], 1);
+        const int i0 = 4 * lane;   // pairs (i, i + 1) with i + 1 < n_c
+        const bool ok = (i0 + 1 >= n_c || key[0] > key[1]) && (i0 + 2 >= n_c || key[1] > key[2]) &&
+                        (i0 + 3 >= n_c || key[2] > key[3]) && (i0 + 4 >= n_c || key[3] > nx);
+        if (!__all_sync(kFull, ok)) sort_keys_exact(key, lane);
+    }
+    uint64_t *keys = reinterpret_cast<uint64_t *>(region + kKeysOffset);
+    float *ps = reinterpret_cast<float *>(region + kPsOffset);
+    reinterpret_cast<ulonglong2 *>(keys)[2 * lane] = make_ulonglong2(key[0], key[1]);
+    reinterpret_cast<ulonglong2 *>(keys)[2 * lane + 1] = make_ulonglong2(key[2], key[3]);
+    reinterpret_cast<float4 *>(ps)[lane] =
+        make_float4(key_p(key[0]), key_p(key[1]), key_p(key[2]), key_p(key[3]));
+    __syncwarp();
+
+    // The list is keys[0..m) (positive probabilities, sorted) followed by
+    // zero-probability tokens in token order, n entries in all.
+    const int m = min(n_pos, K);
+    int n = K;
+    int hit = -1;   // 1 + the walk's position; -1 when it runs past the positives
+    bool fast = true;
+    double P[4];
+    prefix_f64(key, m, lane, P);
+    if (top_p < 1.0f) {
+        const double tpS = (double)top_p * prefix_at(P, m - 1);
+        uint32_t nb = 0u;   // positions not certainly below top_p
+#pragma unroll
+        for (int e = 0; e < 4; e++)
+            if (4 * lane + e < m && !(P[e] * (1.0 + kSumEta) < tpS)) nb |= 1u << e;
+        const int jj = first_flagged(nb);
+        if (jj < 128) {   // 128: the sum never reaches top_p, no cut
+            if (prefix_at(P, jj) * (1.0 - kSumEta) >= tpS) n = jj + 1;
+            else fast = false;
+        }
+    }
+    if (fast && min_p > 0.0f) {
+        if (!(min_p >= 0x1p-100f)) {   // thresholds near the f32 range's end
+            fast = false;
+        } else {   // keep while p_i >= p_0 * min_p
+            const int mm = min(n, m);
+            const double thr = (double)__shfl_sync(kFull, key_p(key[0]), 0) * (double)min_p;
+            uint32_t nk = 0u;   // positions not certainly kept
+#pragma unroll
+            for (int e = 0; e < 4; e++)
+                if (4 * lane + e < mm && !((double)key_p(key[e]) >= thr * (1.0 + kMinpEta)))
+                    nk |= 1u << e;
+            const int jj = first_flagged(nk);
+            if (jj == 128)
+                n = mm;   // every positive kept; the zero tail is not (thresh > 0)
+            else if ((double)key_p_at(key, jj) < thr * (1.0 - kMinpEta))
+                n = jj;
+            else
+                fast = false;
+        }
+    }
+    // one uniform, CDF walk (src/zonos2_generate.cpp:86-92): the first position
+    // whose partial sum reaches u
+    if (fast) {
+        const int len = min(n, m);
+        const double uS = (double)u * prefix_at(P, len - 1);
+        uint32_t nb = 0u;   // positions not certainly below u
+#pragma unroll
+        for (int e = 0; e < 4; e++)
+            if (4 * lane + e < len && !(uS > P[e] * (1.0 + kSumEta))) nb |= 1u << e;
+        const int jj = first_flagged(nb);
+        if (jj < 128) {
+            if (uS <= prefix_at(P, jj) * (1.0 - kSumEta)) hit = jj + 1;
+            else fast = false;
+        }
+    }
+    if (!fast) {   // term by term, as the reference
+        float *pf = reinterpret_cast<float *>(region + kPfOffset);
+        float *q = reinterpret_cast<float *>(region + kQOffset);
+        n = K;
+        if (lane == 0) prefix_sums(ps, pf, m);
+        __syncwarp();
+        float S = pf[m - 1];
+        if (top_p < 1.0f) {
+            const int c = walk_cdf(ps, q, m, S, top_p, lane);
+            if (c > 0) n = c;  // never inside the zero tail: the sum stops growing
+            S = pf[min(n, m) - 1];
+        }
+        if (min_p > 0.0f) {
+            const float thresh = (ps[0] / S) * min_p;
+            const int mm = min(n, m);
+            int jn = minp_cut(ps, mm, S, thresh, lane);
+            if (jn == mm && n > mm) jn = (0.0f >= thresh) ? n : mm;
+            n = jn;
+            S = pf[min(n, m) - 1];
+        }
+        hit = walk_cdf(ps, q, min(n, m), S, u, lane);
+    }
+    int tok = pad;
+    if (lane == 0)
+        tok = pick_token(keys, hit > 0 ? hit - 1 : -1, n, m, n_pos,
+                         reinterpret_cast<uint32_t *>(region + kPosmapOffset), V, pad);
+    return tok;
 }
 
 // Persistent: warp w of CTA b takes work items b + gridDim.x * w + k * W (W warps
@@ -929,7 +1079,7 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
                     const float z1 = ((seenm >> (i + 1)) & 1u) ? fminf(pa.y, pb.y) : x.y;
                     v[i] = ((km >> i) & 1u) ? z0 : -INFINITY;
                     v[i + 1] = ((km >> (i + 1)) & 1u) ? z1 : -INFINITY;
-                    mx = fmaxf(mx, fmaxf(v[i], v[i + 1]));
+                    mx = fmax3(mx, v[i], v[i + 1]);
                 }
                 acc = __fadd_rn(acc2.x, acc2.y);
             }
@@ -1104,126 +1254,137 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
                 // candidates: odd-even transposition rounds finish them; a bitonic
                 // network takes over if 16 rounds do not.
                 if (!oets_desc(ck, lane, 16)) bitonic128_desc(ck, lane);
-                const SmemExpTable tab{exptab};
-                uint64_t key[4];
-                int np = 0;
+                // ---- 6. probabilities to certify decisions with: p~ = 2^(fl(l - M) * c2),
+                // c2 = RN(log2(e) / T), by the hardware exp2.  Against the reference's
+                // p = RN(exp(fl(l - M) / T)): the argument differs by at most three f32
+                // roundings, a relative 3.02 * 2^-24 of |x| = |l - M| / T (so p~ / p by
+                // |x| * 3.02 * 2^-24 relative), the exp2 by less than 2^-20 and the
+                // reference's rounding by 2^-24.  Every candidate lies in a bucket <= bc,
+                // so |x| * log2(e) <= argmax below.
+                const float c2 = (float)(a.inv_temp * 1.4426950408889634);
+                const float argmax =
+                    ((float)bc + 0.52f + fabsf(Msc) * 0x1p-22f) * bw * c2 * 1.0001f;
+                const float eps_p = argmax * (2.2f * 0x1p-24f) + (0x1p-20f + 0x1p-23f);
+                float lv[4], pv[4];
+                uint32_t tk[4];
 #pragma unroll
                 for (int e = 0; e < 4; e++) {
-                    key[e] = 0ull;   // sorts after every candidate
-                    if (4 * lane + e < n_c) {
-                        const int t = (int)(~ck[e] & 1023u);
-                        const float p = row_prob(rowf[t], M, a.inv_temp, tab);
-                        np += p > 0.0f;
-                        key[e] = make_key(p, t);
-                    }
-                }
-                const int n_pos = __reduce_add_sync(kFull, np);
-                {
-                    const uint64_t nx = __shfl_down_sync(kFull, key[0], 1);
-                    const int i0 = 4 * lane;   // pairs (i, i + 1) with i + 1 < n_c
-                    const bool ok = (i0 + 1 >= n_c || key[0] > key[1]) &&
-                                    (i0 + 2 >= n_c || key[1] > key[2]) &&
-                                    (i0 + 3 >= n_c || key[2] > key[3]) &&
-                                    (i0 + 4 >= n_c || key[3] > nx);
-                    if (!__all_sync(kFull, ok)) sort_keys_exact(key, lane);
+                    tk[e] = ~ck[e] & 1023u;
+                    lv[e] = rowf[tk[e]];
+                    pv[e] = 4 * lane + e < n_c ? ex2_approx(__fmul_rn(__fsub_rn(lv[e], M), c2)) : 0.0f;
                 }
                 __syncwarp();   // the row and the stage are free
                 if (cb_nx < NCB) issue(s_nx, cb_nx);
-                uint64_t *keys = reinterpret_cast<uint64_t *>(region + kKeysOffset);
-                float *ps = reinterpret_cast<float *>(region + kPsOffset);
-                reinterpret_cast<ulonglong2 *>(keys)[2 * lane] = make_ulonglong2(key[0], key[1]);
-                reinterpret_cast<ulonglong2 *>(keys)[2 * lane + 1] = make_ulonglong2(key[2], key[3]);
-                reinterpret_cast<float4 *>(ps)[lane] =
-                    make_float4(key_p(key[0]), key_p(key[1]), key_p(key[2]), key_p(key[3]));
-                __syncwarp();
 
-                // ---- 7. top-k / top-p / min-p (src/zonos2_generate.cpp:55-84).  The
-                // list is keys[0..m) (positive probabilities, sorted) followed by
-                // zero-probability tokens in token order, n entries in all.  Every
-                // decision is taken from the exact prefix sums P with the error margin
-                // above (min-p needs none of the sums: the reference divides both sides
-                // of its comparison by the same sum); a row where one is too close to
-                // call is redone term by term, with the reference's running f32 sums.
-                const int m = min(n_pos, K);
+                // The quantized order is the exact (p desc, token asc) order if every
+                // adjacent pair (a, b) has l_a > l_b with t_a < t_b or p_a > p_b for
+                // certain (p is non-decreasing in l), or l_a == l_b (then t_a < t_b: a
+                // shared quantum sorts by token).
+                const float sep = 1.0f + 2.2f * eps_p + 0x1p-22f;
+                bool ok;
+                {
+                    const float ln = __shfl_down_sync(kFull, lv[0], 1);
+                    const float pn = __shfl_down_sync(kFull, pv[0], 1);
+                    const uint32_t tn = __shfl_down_sync(kFull, tk[0], 1);
+                    const int i0 = 4 * lane;
+                    auto pair_ok = [&](float la, uint32_t ta, float pa, float lb, uint32_t tb,
+                                       float pb) {
+                        return (la > lb && (ta < tb || pa > __fmul_rn(pb, sep))) || la == lb;
+                    };
+                    ok = (i0 + 1 >= n_c || pair_ok(lv[0], tk[0], pv[0], lv[1], tk[1], pv[1])) &&
+                         (i0 + 2 >= n_c || pair_ok(lv[1], tk[1], pv[1], lv[2], tk[2], pv[2])) &&
+                         (i0 + 3 >= n_c || pair_ok(lv[2], tk[2], pv[2], lv[3], tk[3], pv[3])) &&
+                         (i0 + 4 >= n_c || pair_ok(lv[3], tk[3], pv[3], ln, tn, pn));
+                }
+                bool fast = __all_sync(kFull, ok) && argmax <= 110.0f;
+
+                // ---- 7. top-k / top-p / min-p (src/zonos2_generate.cpp:55-84) on
+                // prefix sums in 2^-24 fixed point: each term truncated (under 2^-24
+                // each; p_0 = 1, so every sum is >= 1), the sums themselves exact.  A
+                // decision is taken where it clears the threshold by the reference's own
+                // margin plus these errors; any other row goes to the exact form.  Every
+                // candidate has p > 0 here (argmax <= 110), so the list is the first
+                // m = min(n_c, K) candidates.
+                const int m = min(n_c, K);
                 int n = K;
-                int hit = -1;   // 1 + the walk's position; -1 when it runs past the positives
-                bool fast = true;
-                double P[4];
-                prefix_f64(key, m, lane, P);
+                int hit = -1;   // 1 + the walk's position
+                uint32_t P[4];
+                {
+                    uint32_t run = 0u;
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        run += 4 * lane + e < m ? __float2uint_rz(pv[e] * 0x1p24f) : 0u;
+                        P[e] = run;
+                    }
+                    uint32_t incl = run;
+#pragma unroll
+                    for (int o = 1; o < 32; o <<= 1) {
+                        const uint32_t y = __shfl_up_sync(kFull, incl, o);
+                        if (lane >= o) incl += y;
+                    }
+                    const uint32_t excl = incl - run;
+#pragma unroll
+                    for (int e = 0; e < 4; e++) P[e] += excl;
+                }
+                // |sum~ / sum - 1| <= es; the thresholds below are f32 products of at
+                // most four roundings, which the 2^-21 covers
+                const float es = eps_p + (float)n_c * 0x1p-24f;
+                const float eta = (float)(kSumEta * 1.01) + 2.2f * es + (0x1p-21f + 0x1p-30f);
+                // Each decision counts the positions certainly below / not certainly
+                // above its threshold (P is non-decreasing along the list, p~ the same up
+                // to its error): equal counts settle it, and the count is the position.
+                auto P_at = [&](int i) { return __shfl_sync(kFull, sel4u(P, i & 3), i >> 2); };
                 if (a.top_p < 1.0f) {
-                    const double tpS = (double)a.top_p * prefix_at(P, m - 1);
-                    uint32_t nb = 0u;   // positions not certainly below top_p
+                    const float tpS = a.top_p * (float)P_at(m - 1);
+                    const uint32_t lo = __float2uint_ru(tpS * (1.0f - eta));   // P < lo: below
+                    const uint32_t hi = __float2uint_ru(tpS * (1.0f + 1.01f * eta));   // P >= hi: reached
+                    int c = 0;
 #pragma unroll
                     for (int e = 0; e < 4; e++)
-                        if (4 * lane + e < m && !(P[e] * (1.0 + kSumEta) < tpS)) nb |= 1u << e;
-                    const int jj = first_flagged(nb);
-                    if (jj < 128) {   // 128: the sum never reaches top_p, no cut
-                        if (prefix_at(P, jj) * (1.0 - kSumEta) >= tpS) n = jj + 1;
-                        else fast = false;
+                        if (4 * lane + e < m) c += (P[e] < lo ? 1 : 0) + (P[e] < hi ? 0x10000 : 0);
+                    c = __reduce_add_sync(kFull, c);
+                    const int c_lo = c & 0xffff, c_hi = c >> 16;
+                    if (c_lo < m) {   // else the sum never reaches top_p: no cut
+                        n = c_lo + 1;
+                        fast = fast && c_lo == c_hi;
                     }
                 }
-                if (fast && a.min_p > 0.0f) {
-                    if (!(a.min_p >= 0x1p-100f)) {   // thresholds near the f32 range's end
-                        fast = false;
-                    } else {   // keep while p_i >= p_0 * min_p
-                        const int mm = min(n, m);
-                        const double thr =
-                            (double)__shfl_sync(kFull, key_p(key[0]), 0) * (double)a.min_p;
-                        uint32_t nk = 0u;   // positions not certainly kept
+                if (a.min_p > 0.0f) {   // keep while p_i >= p_0 * min_p, p_0 = 1
+                    const int mm = min(n, m);
+                    const float em = (float)(kMinpEta * 1.01) + 2.2f * eps_p + 0x1p-22f;
+                    const float keep = __fmul_rn(a.min_p, 1.0f + em);
+                    const float drop = __fmul_rn(a.min_p, 1.0f - em);
+                    int c = 0;
 #pragma unroll
-                        for (int e = 0; e < 4; e++)
-                            if (4 * lane + e < mm && !((double)key_p(key[e]) >= thr * (1.0 + kMinpEta)))
-                                nk |= 1u << e;
-                        const int jj = first_flagged(nk);
-                        if (jj == 128)
-                            n = mm;   // every positive kept; the zero tail is not (thresh > 0)
-                        else if ((double)key_p_at(key, jj) < thr * (1.0 - kMinpEta))
-                            n = jj;
-                        else
-                            fast = false;
-                    }
+                    for (int e = 0; e < 4; e++)
+                        if (4 * lane + e < mm) c += (pv[e] >= keep ? 1 : 0) + (pv[e] >= drop ? 0x10000 : 0);
+                    c = __reduce_add_sync(kFull, c);
+                    n = c & 0xffff;   // the first position dropped (mm: none)
+                    fast = fast && n == (c >> 16) && a.min_p >= 0x1p-100f;
                 }
                 // ---- 8. one uniform, CDF walk (src/zonos2_generate.cpp:86-92): the
                 // first position whose partial sum reaches u
-                if (fast) {
+                {
                     const int len = min(n, m);
-                    const double uS = (double)u * prefix_at(P, len - 1);
-                    uint32_t nb = 0u;   // positions not certainly below u
+                    const float uS = u * (float)P_at(max(len, 1) - 1);
+                    const uint32_t lo = __float2uint_ru(uS * (1.0f - eta));
+                    const uint32_t hi = __float2uint_ru(uS * (1.0f + 1.01f * eta));
+                    int c = 0;
 #pragma unroll
                     for (int e = 0; e < 4; e++)
-                        if (4 * lane + e < len && !(uS > P[e] * (1.0 + kSumEta))) nb |= 1u << e;
-                    const int jj = first_flagged(nb);
-                    if (jj < 128) {
-                        if (uS <= prefix_at(P, jj) * (1.0 - kSumEta)) hit = jj + 1;
-                        else fast = false;
-                    }
+                        if (4 * lane + e < len) c += (P[e] < lo ? 1 : 0) + (P[e] < hi ? 0x10000 : 0);
+                    c = __reduce_add_sync(kFull, c);
+                    hit = (c & 0xffff) + 1;
+                    fast = fast && len > 0 && hit <= len && (c & 0xffff) == (c >> 16);
                 }
-                if (!fast) {   // term by term, as the reference
-                    float *pf = reinterpret_cast<float *>(region + kPfOffset);
-                    float *q = reinterpret_cast<float *>(region + kQOffset);
-                    n = K;
-                    if (lane == 0) prefix_sums(ps, pf, m);
-                    __syncwarp();
-                    float S = pf[m - 1];
-                    if (a.top_p < 1.0f) {
-                        const int c = walk_cdf(ps, q, m, S, a.top_p, lane);
-                        if (c > 0) n = c;  // never inside the zero tail: the sum stops growing
-                        S = pf[min(n, m) - 1];
-                    }
-                    if (a.min_p > 0.0f) {
-                        const float thresh = (ps[0] / S) * a.min_p;
-                        const int mm = min(n, m);
-                        int jn = minp_cut(ps, mm, S, thresh, lane);
-                        if (jn == mm && n > mm) jn = (0.0f >= thresh) ? n : mm;
-                        n = jn;
-                        S = pf[min(n, m) - 1];
-                    }
-                    hit = walk_cdf(ps, q, min(n, m), S, u, lane);
+                if (fast) {
+                    const int pos = hit - 1;
+                    tok = (int)__shfl_sync(kFull, sel4u(tk, pos & 3), pos >> 2);
+                } else {
+                    tok = exact_decide(region, exptab, n_c, K, V, a.pad_id, a.top_p, a.min_p,
+                                       a.inv_temp, M, u, lane, lv[0], lv[1], lv[2], lv[3], tk[0],
+                                       tk[1], tk[2], tk[3]);
                 }
-                if (lane == 0)
-                    tok = pick_token(keys, hit > 0 ? hit - 1 : -1, n, m, n_pos,
-                                     reinterpret_cast<uint32_t *>(region + kPosmapOffset), V,
-                                     a.pad_id);
             }
         } else {
             __syncwarp();   // the row is free
