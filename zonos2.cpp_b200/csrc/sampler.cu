@@ -85,7 +85,8 @@ namespace {
 // General path: up to 1024 keys over [0, 8192) (no copy is in flight then).
 constexpr int kRegion = 8192;
 constexpr int kWarpStride = kRegion + 144;
-constexpr int kCtaHeader = 512;          // 2^(j/64), j < 64, shared by the CTA's warps
+constexpr int kCtaHeader = 528;          // 2^(j/64), j < 64, shared by the CTA's warps; the item counter
+constexpr int kCtrOffset = 512;
 constexpr int kRowOffset = 0;
 constexpr int kBktOffset = 4096;
 constexpr int kKeysOffset = 4096;
@@ -757,6 +758,14 @@ constexpr double kSumEta = 640.0 * 0x1p-24;
 // p_i < p_0 * min_p * (1 - 3 * 2^-24) drops it; the margin is taken 5x.
 constexpr double kMinpEta = 16.0 * 0x1p-24;
 
+// The same bound for one list of len terms: the sum takes len - 1 roundings, the
+// quotients one each, the running sum up to position i < len another i; the
+// factor covers the second-order terms.
+__device__ __forceinline__ float sum_eta(int len)
+{
+    return (float)(2 * len) * (1.01f * 0x1p-24f);
+}
+
 // The probability at sorted position i, in every lane.
 __device__ __forceinline__ float key_p_at(const uint64_t key[4], int i)
 {
@@ -897,11 +906,13 @@ __device__ __noinline__ int exact_decide(unsigned char *region, const double *ex
     return tok;
 }
 
-// Persistent: warp w of CTA b takes work items b + gridDim.x * w + k * W (W warps
-// in the grid).  Items run codebook-major (item cb * n_streams + s is row
-// s * n_cb + cb), so a warp's items cycle through the codebooks whatever the grid,
-// and a row's cost (delay-forced codebooks are cheap) does not stick to one warp.
-// While a row is sorted and decided, the bulk copy of the warp's next row lands.
+// Persistent: CTA b owns work items b + k * gridDim.x, k = 0, 1, ...; warp w starts
+// on k = w and then takes the CTA's next free k from a shared counter, so a warp
+// held up by a slow row (the exact form, a general-path row) leaves the rest of
+// its CTA's rows to its siblings.  Items run codebook-major (item cb * n_streams + s
+// is row s * n_cb + cb), so every CTA sees every codebook and a row's cost
+// (delay-forced codebooks are cheap) does not stick to one CTA.  While a row is
+// sorted and decided, the bulk copy of the warp's next row lands.
 __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(const SampleArgs a)
 {
     extern __shared__ __align__(16) unsigned char smem[];
@@ -913,7 +924,9 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
     uint32_t *hist = reinterpret_cast<uint32_t *>(region + kHistOffset);
     uint32_t *bkt = reinterpret_cast<uint32_t *>(region + kBktOffset);
     const uint32_t bar = smem_u32(region + kBarOffset);
+    unsigned *next_k = reinterpret_cast<unsigned *>(smem + kCtrOffset);
     if (threadIdx.x < 64) exptab[threadIdx.x] = exp2_64th(threadIdx.x);
+    if (threadIdx.x == 0) *next_k = (unsigned)kWarps;
     if (lane == 0) {
         mbar_init(bar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -930,13 +943,30 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
     const uint32_t row_bytes = 4u * (uint32_t)V;
     const uint32_t *slots = reinterpret_cast<const uint32_t *>(a.codes);
 
-    // work items: (s, cb) of item it, advanced by the grid's warp count
-    const long long step = (long long)gridDim.x * kWarps;
-    const int step_cb = (int)(step / S_);
-    const int step_s = (int)(step - (long long)step_cb * S_);
-    const long long it0 = blockIdx.x + (long long)gridDim.x * w;
-    int cb = (int)(it0 / S_);
-    int s = (int)(it0 - (long long)cb * S_);
+    // work item it -> (s, cb), codebook-major: the quotient by an f64 reciprocal,
+    // corrected by one either way
+    const long long n_items = (long long)S_ * NCB;
+    const double inv_S = 1.0 / (double)S_;
+    auto item_at = [&](long long it, int &s2, int &cb2) {
+        if (it >= n_items) {
+            s2 = 0;
+            cb2 = NCB;   // no item
+            return;
+        }
+        long long q = (long long)((double)it * inv_S);
+        long long rem = it - q * S_;
+        if (rem < 0) {
+            q--;
+            rem += S_;
+        } else if (rem >= S_) {
+            q++;
+            rem -= S_;
+        }
+        cb2 = (int)q;
+        s2 = (int)rem;
+    };
+    int s, cb;
+    item_at(blockIdx.x + (long long)gridDim.x * w, s, cb);
 
     uint32_t phase = 0u;
     bool drawn = false;     // the draw grid has been waited for
@@ -962,10 +992,12 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
     while (cb < NCB) {
         const long long r = (long long)s * NCB + cb;
         const float *lrow = a.logits + r * a.row_stride;
-        int s_nx = s + step_s, cb_nx = cb + step_cb;
-        if (s_nx >= S_) {
-            s_nx -= S_;
-            cb_nx++;
+        int s_nx, cb_nx;
+        {
+            unsigned k = 0u;
+            if (lane == 0) k = atomicAdd(next_k, 1u);
+            k = __shfl_sync(kFull, k, 0);
+            item_at(blockIdx.x + (long long)gridDim.x * k, s_nx, cb_nx);
         }
         if (!pending) issue(s, cb);
 
@@ -1258,13 +1290,14 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
                 // c2 = RN(log2(e) / T), by the hardware exp2.  Against the reference's
                 // p = RN(exp(fl(l - M) / T)): the argument differs by at most three f32
                 // roundings, a relative 3.02 * 2^-24 of |x| = |l - M| / T (so p~ / p by
-                // |x| * 3.02 * 2^-24 relative), the exp2 by less than 2^-20 and the
-                // reference's rounding by 2^-24.  Every candidate lies in a bucket <= bc,
-                // so |x| * log2(e) <= argmax below.
+                // |x| * 3.02 * 2^-24 relative), the exp2 by less than 2^-21 (its largest
+                // error over every f32 argument in [-126, 0], measured on this part, is
+                // 2^-22.7) and the reference's rounding by 2^-24.  Every candidate lies in
+                // a bucket <= bc, so |x| * log2(e) <= argmax below.
                 const float c2 = (float)(a.inv_temp * 1.4426950408889634);
                 const float argmax =
                     ((float)bc + 0.52f + fabsf(Msc) * 0x1p-22f) * bw * c2 * 1.0001f;
-                const float eps_p = argmax * (2.2f * 0x1p-24f) + (0x1p-20f + 0x1p-23f);
+                const float eps_p = argmax * (2.2f * 0x1p-24f) + (0x1p-21f + 0x1p-23f);
                 float lv[4], pv[4];
                 uint32_t tk[4];
 #pragma unroll
@@ -1299,8 +1332,8 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
                 bool fast = __all_sync(kFull, ok) && argmax <= 110.0f;
 
                 // ---- 7. top-k / top-p / min-p (src/zonos2_generate.cpp:55-84) on
-                // prefix sums in 2^-24 fixed point: each term truncated (under 2^-24
-                // each; p_0 = 1, so every sum is >= 1), the sums themselves exact.  A
+                // prefix sums in 2^-24 fixed point: each term rounded to nearest (within
+                // 2^-25; p_0 = 1, so every sum is >= 1), the sums themselves exact.  A
                 // decision is taken where it clears the threshold by the reference's own
                 // margin plus these errors; any other row goes to the exact form.  Every
                 // candidate has p > 0 here (argmax <= 110), so the list is the first
@@ -1313,7 +1346,7 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
                     uint32_t run = 0u;
 #pragma unroll
                     for (int e = 0; e < 4; e++) {
-                        run += 4 * lane + e < m ? __float2uint_rz(pv[e] * 0x1p24f) : 0u;
+                        run += 4 * lane + e < m ? __float2uint_rn(pv[e] * 0x1p24f) : 0u;
                         P[e] = run;
                     }
                     uint32_t incl = run;
@@ -1326,16 +1359,19 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
 #pragma unroll
                     for (int e = 0; e < 4; e++) P[e] += excl;
                 }
-                // |sum~ / sum - 1| <= es; the thresholds below are f32 products of at
-                // most four roundings, which the 2^-21 covers
-                const float es = eps_p + (float)n_c * 0x1p-24f;
-                const float eta = (float)(kSumEta * 1.01) + 2.2f * es + (0x1p-21f + 0x1p-30f);
+                // |sum~ / sum - 1| <= es.  The reference's running quotient sum over a
+                // list of len terms is P_i / S * (1 + d), |d| <= (2 len - 1) * 2^-24 * 1.001
+                // (sum_eta), against the exact sums; the f32 thresholds below take at
+                // most four roundings (2^-22).
+                const float es = eps_p + (float)n_c * 0x1p-25f;
+                const float eta_c = 2.2f * es + (0x1p-22f + 0x1p-30f);
                 // Each decision counts the positions certainly below / not certainly
                 // above its threshold (P is non-decreasing along the list, p~ the same up
                 // to its error): equal counts settle it, and the count is the position.
                 auto P_at = [&](int i) { return __shfl_sync(kFull, sel4u(P, i & 3), i >> 2); };
                 if (a.top_p < 1.0f) {
                     const float tpS = a.top_p * (float)P_at(m - 1);
+                    const float eta = sum_eta(m) + eta_c;
                     const uint32_t lo = __float2uint_ru(tpS * (1.0f - eta));   // P < lo: below
                     const uint32_t hi = __float2uint_ru(tpS * (1.0f + 1.01f * eta));   // P >= hi: reached
                     int c = 0;
@@ -1367,6 +1403,7 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
                 {
                     const int len = min(n, m);
                     const float uS = u * (float)P_at(max(len, 1) - 1);
+                    const float eta = sum_eta(len) + eta_c;
                     const uint32_t lo = __float2uint_ru(uS * (1.0f - eta));
                     const uint32_t hi = __float2uint_ru(uS * (1.0f + 1.01f * eta));
                     int c = 0;
