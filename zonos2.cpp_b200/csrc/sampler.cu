@@ -745,26 +745,22 @@ __device__ __forceinline__ float ex2_approx(float a)
     return r;
 }
 
-// A partial sum the reference accumulates term by term in f32 over sorted
-// probabilities p_j (j <= i < 128), each divided by an f32 sum S' of at most 128
-// of them, is P_i / S * (1 + d) with P_i, S the exact sums and
-// |d| <= (i + 128 + 2) * 2^-24 (+ O(2^-48)): one rounding per division, per
-// add, and the sums' own rounding.  Decisions clear of the threshold by this
-// margin (taken 2.5x) equal the reference's; the rest are made term by term.
-constexpr double kSumEta = 640.0 * 0x1p-24;
+// A partial sum the reference accumulates term by term in f32 over a sorted list
+// of len probabilities p_j, each divided by the list's own f32 sum S', is at
+// position i < len P_i / S * (1 + d), with P_i, S the exact sums and
+// |d| <= (len - 1 + 1 + i) * 2^-24 * (1 + O(2^-24)): len - 1 roundings in S', one
+// per division, i in the running sum.  sum_eta(len) bounds it for every i < len
+// (the factor covers the second-order terms); decisions clear of the threshold
+// by this margin equal the reference's, the rest are made term by term.
+__device__ __forceinline__ float sum_eta(int len)
+{
+    return (float)(2 * len) * (1.01f * 0x1p-24f);
+}
 
 // min-p keeps position i while fl(p_i / S) >= fl(fl(p_0 / S) * min_p); the sum S
 // cancels, so p_i >= p_0 * min_p * (1 + 2^-24) keeps it and
 // p_i < p_0 * min_p * (1 - 3 * 2^-24) drops it; the margin is taken 5x.
 constexpr double kMinpEta = 16.0 * 0x1p-24;
-
-// The same bound for one list of len terms: the sum takes len - 1 roundings, the
-// quotients one each, the running sum up to position i < len another i; the
-// factor covers the second-order terms.
-__device__ __forceinline__ float sum_eta(int len)
-{
-    return (float)(2 * len) * (1.01f * 0x1p-24f);
-}
 
 // The probability at sorted position i, in every lane.
 __device__ __forceinline__ float key_p_at(const uint64_t key[4], int i)
@@ -832,13 +828,14 @@ __device__ __noinline__ int exact_decide(unsigned char *region, const double *ex
     prefix_f64(key, m, lane, P);
     if (top_p < 1.0f) {
         const double tpS = (double)top_p * prefix_at(P, m - 1);
+        const double eta = (double)sum_eta(m) + 0x1p-40;
         uint32_t nb = 0u;   // positions not certainly below top_p
 #pragma unroll
         for (int e = 0; e < 4; e++)
-            if (4 * lane + e < m && !(P[e] * (1.0 + kSumEta) < tpS)) nb |= 1u << e;
+            if (4 * lane + e < m && !(P[e] * (1.0 + eta) < tpS)) nb |= 1u << e;
         const int jj = first_flagged(nb);
         if (jj < 128) {   // 128: the sum never reaches top_p, no cut
-            if (prefix_at(P, jj) * (1.0 - kSumEta) >= tpS) n = jj + 1;
+            if (prefix_at(P, jj) * (1.0 - eta) >= tpS) n = jj + 1;
             else fast = false;
         }
     }
@@ -866,14 +863,15 @@ __device__ __noinline__ int exact_decide(unsigned char *region, const double *ex
     // whose partial sum reaches u
     if (fast) {
         const int len = min(n, m);
-        const double uS = (double)u * prefix_at(P, len - 1);
+        const double uS = (double)u * prefix_at(P, max(len, 1) - 1);
+        const double eta = (double)sum_eta(len) + 0x1p-40;
         uint32_t nb = 0u;   // positions not certainly below u
 #pragma unroll
         for (int e = 0; e < 4; e++)
-            if (4 * lane + e < len && !(uS > P[e] * (1.0 + kSumEta))) nb |= 1u << e;
+            if (4 * lane + e < len && !(uS > P[e] * (1.0 + eta))) nb |= 1u << e;
         const int jj = first_flagged(nb);
         if (jj < 128) {
-            if (uS <= prefix_at(P, jj) * (1.0 - kSumEta)) hit = jj + 1;
+            if (uS <= prefix_at(P, jj) * (1.0 - eta)) hit = jj + 1;
             else fast = false;
         }
     }
