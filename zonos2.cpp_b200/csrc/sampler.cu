@@ -99,8 +99,10 @@ constexpr int kPosmapOffset = kRegion;
 constexpr int kBarOffset = kRegion + 128;
 constexpr int kBuckets = 128;    // gap buckets: 0..126 finite, 127 marks a masked slot
 constexpr int kRegSortMax = 128; // candidates sorted in registers (four per lane)
-constexpr int kWarps = 9;       // warps per CTA
-constexpr int kCtasPerSm = 3;   // 27 warps per SM: shared memory and <= 72 registers
+constexpr int kWarps = 27;      // warps per CTA: one CTA per SM, so the rows of a whole SM are
+                                // shared out by one counter (9-warp CTAs, three per SM, left
+                                // more of the SM idle at the end of a launch)
+constexpr int kCtasPerSm = 1;   // shared memory and <= 72 registers
 constexpr unsigned long long kWaitNs = 2000000000ull;
 
 enum : int { kErrTimeout = 1 };
@@ -1544,10 +1546,11 @@ cudaError_t launch_sample(const SampleArgs &a, cudaStream_t stream)
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
 
+    // One CTA per SM, or per row when there are fewer rows than SMs: a small batch
+    // spreads over as many SMs as it has rows.
     const long long rows = (long long)a.n_streams * a.n_cb;
-    const long long need = (rows + kWarps - 1) / kWarps;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(need < cap ? need : cap));
+    cfg.gridDim = dim3((unsigned)(rows < cap ? rows : cap));
     cfg.blockDim = dim3(32 * kWarps);
     cfg.dynamicSmemBytes = sample_smem_bytes();
     cfg.stream = stream;
