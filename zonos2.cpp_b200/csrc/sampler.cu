@@ -80,11 +80,10 @@ namespace {
 //   [5120, 5632)   128 bucket counters, then the sorted probabilities
 //   [5632, 6656)   compacted candidates (logit, token); after the sort the
 //                  prefix sums [5632, 6144) and p / sum [6144, 6656)
-//   [8192, 8320)   1024-bit map of positive tokens (zero-tail fall-through)
-//   [8320, 8328)   the row copy's mbarrier
+//   [8192, 8200)   the row copy's mbarrier
 // General path: up to 1024 keys over [0, 8192) (no copy is in flight then).
 constexpr int kRegion = 8192;
-constexpr int kWarpStride = kRegion + 144;
+constexpr int kWarpStride = kRegion + 16;
 constexpr int kCtaHeader = 528;          // 2^(j/64), j < 64, shared by the CTA's warps; the item counter
 constexpr int kCtrOffset = 512;
 constexpr int kRowOffset = 0;
@@ -95,11 +94,10 @@ constexpr int kPsOffset = 5120;
 constexpr int kStageOffset = 5632;
 constexpr int kPfOffset = 5632;
 constexpr int kQOffset = 6144;
-constexpr int kPosmapOffset = kRegion;
-constexpr int kBarOffset = kRegion + 128;
+constexpr int kBarOffset = kRegion;
 constexpr int kBuckets = 128;    // gap buckets: 0..126 finite, 127 marks a masked slot
 constexpr int kRegSortMax = 128; // candidates sorted in registers (four per lane)
-constexpr int kWarps = 27;      // warps per CTA: one CTA per SM, so the rows of a whole SM are
+constexpr int kWarps = 28;      // warps per CTA: one CTA per SM, so the rows of a whole SM are
                                 // shared out by one counter (9-warp CTAs, three per SM, left
                                 // more of the SM idle at the end of a launch)
 constexpr int kCtasPerSm = 1;   // shared memory and <= 72 registers
@@ -361,38 +359,40 @@ __device__ __forceinline__ int minp_cut(const float *ps, int mm, float S, float 
 }
 
 // The (want)-th token, in token order, outside the positive set of a row
-// (keys[0..n_pos)); one lane.
-__device__ __noinline__ int zero_tail_token(const uint64_t *keys, int n_pos, uint32_t *posmap,
-                                            int V, int want)
+// (keys[0..n_pos)); -1 if there is none.  The whole warp: lane l holds the
+// positive bits of tokens 32l .. 32l + 31.
+__device__ __noinline__ int zero_tail_token(const uint64_t *keys, int n_pos, int V, int want,
+                                            int lane)
 {
-    for (int w = 0; w < 32; w++) posmap[w] = 0u;
+    uint32_t pm = 0u;
     for (int i = 0; i < n_pos; i++) {
         const int t = key_tok(keys[i]);
-        posmap[t >> 5] |= 1u << (t & 31);
+        if ((t >> 5) == lane) pm |= 1u << (t & 31);
     }
-    for (int w = 0; w < 32; w++) {
-        const int lo = 32 * w;
-        if (lo >= V) break;
-        const uint32_t valid = V - lo >= 32 ? ~0u : ((1u << (V - lo)) - 1u);
-        uint32_t z = ~posmap[w] & valid;
-        const int c = __popc(z);
-        if (want < c) {
-            for (; want > 0; want--) z &= z - 1;
-            return lo + __ffs(z) - 1;
-        }
-        want -= c;
+    const int lo = 32 * lane;
+    const uint32_t valid = lo >= V ? 0u : (V - lo >= 32 ? ~0u : ((1u << (V - lo)) - 1u));
+    uint32_t z = ~pm & valid;
+    const int c = __popc(z);
+    const int incl = warp_incl_scan(c, lane);
+    const bool mine = want >= incl - c && want < incl;
+    const uint32_t b = __ballot_sync(kFull, mine);
+    int tok = -1;
+    if (mine) {
+        for (int k = want - (incl - c); k > 0; k--) z &= z - 1;
+        tok = lo + __ffs(z) - 1;
     }
-    return -1;
+    return b ? __shfl_sync(kFull, tok, __ffs(b) - 1) : -1;
 }
 
 // The token once the list is settled: position pos, or the last of n entries
 // (a zero-probability token when the walk fell past the m positive ones).
+// The whole warp, with warp-uniform arguments.
 __device__ __forceinline__ int pick_token(const uint64_t *keys, int pos, int n, int m, int n_pos,
-                                          uint32_t *posmap, int V, int pad)
+                                          int V, int pad, int lane)
 {
     const int m3 = min(n, m);
     if (pos >= 0) return key_tok(keys[pos]);
-    if (n > m3) return zero_tail_token(keys, n_pos, posmap, V, n - 1 - m3);
+    if (n > m3) return zero_tail_token(keys, n_pos, V, n - 1 - m3, lane);
     return n > 0 ? key_tok(keys[n - 1]) : pad;
 }
 
@@ -405,9 +405,9 @@ struct RowKnobs {
 };
 
 // The general path for rows the common path does not take (top-k off, more
-// than 256 candidates): candidates compacted from a fresh read of the logits,
+// than 128 candidates): candidates compacted from a fresh read of the logits,
 // bitonic sort, sums recomputed from the sorted keys.  Returns the token in
-// lane 0.
+// every lane.
 __device__ __noinline__ int general_path(const RowKnobs &kn, unsigned char *region,
                                          const float *lrow, uint32_t selm, int n_c, float M,
                                          uint32_t seenm, uint32_t allowm, int lane, float u)
@@ -497,10 +497,9 @@ __device__ __noinline__ int general_path(const RowKnobs &kn, unsigned char *regi
         if (lane == 0) S = seq_sum(ent, min(n, m));
         S = __shfl_sync(kFull, S, 0);
     }
-    int tok = kn.pad;
+    int pos = -1;
     if (lane == 0) {
         float cum = 0.0f;
-        int pos = -1;
         for (int i = 0; i < min(n, m); i++) {
             cum += key_p(ent[i]) / S;
             if (u <= cum) {
@@ -508,10 +507,9 @@ __device__ __noinline__ int general_path(const RowKnobs &kn, unsigned char *regi
                 break;
             }
         }
-        tok = pick_token(ent, pos, n, m, n_pos,
-                         reinterpret_cast<uint32_t *>(region + kPosmapOffset), kn.V, kn.pad);
     }
-    return tok;
+    pos = __shfl_sync(kFull, pos, 0);
+    return pick_token(ent, pos, n, m, n_pos, kn.V, kn.pad, lane);
 }
 
 }  // namespace
@@ -783,7 +781,7 @@ __device__ __noinline__ void sort_keys_exact(uint64_t key[4], int lane)
 // quantized order breaks theirs); decisions come from exact f64 prefix sums
 // where the reference's margin allows, else term by term with the reference's
 // f32 sums.  The row's logits are no longer in shared memory: the next row's
-// copy may be landing there.  Returns the token in lane 0.
+// copy may be landing there.  Returns the token in every lane.
 __device__ __noinline__ int exact_decide(unsigned char *region, const double *exptab, int n_c, int K,
                                          int V, int pad, float top_p, float min_p, double inv_temp,
                                          float M, float u, int lane, float l0, float l1, float l2,
@@ -899,11 +897,7 @@ __device__ __noinline__ int exact_decide(unsigned char *region, const double *ex
         }
         hit = walk_cdf(ps, q, min(n, m), S, u, lane);
     }
-    int tok = pad;
-    if (lane == 0)
-        tok = pick_token(keys, hit > 0 ? hit - 1 : -1, n, m, n_pos,
-                         reinterpret_cast<uint32_t *>(region + kPosmapOffset), V, pad);
-    return tok;
+    return pick_token(keys, hit > 0 ? hit - 1 : -1, n, m, n_pos, V, pad, lane);
 }
 
 // Persistent: CTA b owns work items b + k * gridDim.x, k = 0, 1, ...; warp w starts
