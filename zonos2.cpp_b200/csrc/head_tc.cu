@@ -114,6 +114,17 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
         : "memory");
 }
 
+// One tile of shared memory -> global through the tensor map (rows past the
+// tensor's end are not written); completes in this thread's bulk group.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, uint32_t src, int x, int y)
+{
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y), "r"(src)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
 __device__ __forceinline__ void prefetch_map(const CUtensorMap *map)
 {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -184,6 +195,7 @@ struct TcArgs {
     float *out;  // [batch][n_cb * vocab], or [batch / 2][..] with cfg
     int cfg;     // rows 2s, 2s+1 (conditional, unconditional) blend into out row s
     float cfg_scale;
+    int out_rows;   // rows of out: batch, or batch / 2 with cfg
 };
 
 // The epilogue's store of one 32-column chunk of row `row` (lane = row's lane in
@@ -191,6 +203,23 @@ struct TcArgs {
 // classifier-free guidance the blend u + s * (c - u) of the pair, taken from
 // the neighbouring lane and stored by the even lane as output row s
 // (src/zonos2_generate.cpp:178-183).
+// The same chunk's 32 output values of this lane's row (every lane takes part:
+// the guidance blend reads the neighbouring lane).
+__device__ __forceinline__ void finish_chunk(const TcArgs &args, const uint32_t (&r)[32], float k2,
+                                             float (&o)[32])
+{
+    const float cap = args.softcap;
+#pragma unroll
+    for (int i = 0; i < 32; i++) {
+        const float l = __uint_as_float(r[i]);
+        o[i] = cap > 0.0f ? softcap_fast(l, cap, k2) : l;
+        if (args.cfg) {
+            const float u = __shfl_xor_sync(kFull, o[i], 1);
+            o[i] = __fadd_rn(u, __fmul_rn(args.cfg_scale, __fsub_rn(o[i], u)));
+        }
+    }
+}
+
 __device__ __forceinline__ void store_chunk(const TcArgs &args, const uint32_t (&r)[32], int row,
                                             size_t col, float k2)
 {
@@ -474,7 +503,8 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t bar)
 template <int STAGES>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     head_tc2_kernel(const __grid_constant__ CUtensorMap map_a,
-                    const __grid_constant__ CUtensorMap map_b, const TcArgs args)
+                    const __grid_constant__ CUtensorMap map_b,
+                    const __grid_constant__ CUtensorMap map_o, const TcArgs args)
 {
     constexpr int BN = 256;                    // N of the pair's tile; each CTA holds 128 B rows
     constexpr uint32_t kABytes = kBM * kBK * 2;
@@ -487,7 +517,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * kStageBytes);
+    // stages, then 4 KB of output staging per epilogue warp, then the barriers
+    uint64_t *bars =
+        reinterpret_cast<uint64_t *>(smem + STAGES * kStageBytes + (kEpiThreads / 32) * 4096);
     // bars: full[STAGES], empty[STAGES], tfull[2], tempty[2]; the TMEM slot
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 4);
     __shared__ int s_abort;
@@ -514,6 +546,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         prefetch_map(&map_a);
         prefetch_map(&map_b);
+        prefetch_map(&map_o);
     }
     if (warp == 1) {   // both CTAs, same warp: one allocation across the pair
         asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -605,10 +638,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             if (!ok) s_abort = 1;
         }
     } else if (warp >= 2) {
-        // ---- epilogue: this CTA's 128 accumulator rows -> softcap -> global
+        // ---- epilogue: this CTA's 128 accumulator rows -> softcap -> global.  Each
+        // warp stages a 32 x 32 chunk in its own 4 KB of shared memory (128-byte
+        // swizzle: 16-byte piece c of row r at r * 128 + (c ^ (r & 7)) * 16) and
+        // one lane stores it with a tensor copy, whole 128-byte row pieces at a
+        // time, while the warp goes on to the next chunk.
         const int q = warp & 3;             // the TMEM lane quarter this warp may read
         const int half = (warp - 2) >> 2;   // which half of the tile's columns
         const uint32_t tempty0 = peer_addr(tempty(0), 0), tempty1 = peer_addr(tempty(1), 0);
+        const uint32_t stage_o = smem_u32(smem + STAGES * kStageBytes + (warp - 2) * 4096);
+        const int orow = args.cfg ? lane >> 1 : lane;   // this lane's row in the chunk
+        const bool owner = !args.cfg || (lane & 1) == 0;
         int local = 0;
         for (int tile = pair; tile < n_tiles; tile += n_pairs, local++) {
             const int acc = local & 1;
@@ -620,18 +660,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             if (*(volatile int *)&s_abort) break;
             tc_fence_after();
             const int mt = tile % tiles_m2, nt = tile / tiles_m2;
-            const int row = mt * 2 * kBM + (int)rank * kBM + 32 * q + lane;
+            const int row0 = mt * 2 * kBM + (int)rank * kBM + 32 * q;   // the warp's first row
+            const int y0 = args.cfg ? row0 >> 1 : row0;                  // its first output row
             const float k2 = 2.0f * 1.4426950408889634f / args.softcap;   // 2 log2(e) / cap
 #pragma unroll 1
             for (int ch = half * (BN / 64); ch < (half + 1) * (BN / 64); ch++) {
                 uint32_t r[32];
                 tmem_ld32(tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BN + 32 * ch), r);
-                store_chunk(args, r, row, (size_t)nt * BN + 32 * ch, k2);
+                float o[32];
+                finish_chunk(args, r, k2, o);
+                if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+                __syncwarp();   // the previous chunk has left the staging buffer
+                if (owner) {
+#pragma unroll
+                    for (int c = 0; c < 8; c++)
+                        asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(
+                                         stage_o + orow * 128 + ((c ^ (orow & 7)) << 4)),
+                                     "f"(o[4 * c]), "f"(o[4 * c + 1]), "f"(o[4 * c + 2]),
+                                     "f"(o[4 * c + 3])
+                                     : "memory");
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0 && y0 < args.out_rows)
+                    tma_store_2d(&map_o, stage_o, nt * BN + 32 * ch, y0);
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(acc ? tempty1 : tempty0);
         }
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        __syncwarp();
     }
 
     tc_fence_before();
@@ -679,6 +738,22 @@ bool make_map(CUtensorMap *m, const void *base, uint64_t rows, uint64_t cols, ui
            CUDA_SUCCESS;
 }
 
+// 2-D f32 tensor map over rows x cols (cols contiguous), box 32 cols x box_rows,
+// 128-byte swizzle (the epilogue's staging layout).
+bool make_map_f32(CUtensorMap *m, void *base, uint64_t rows, uint64_t cols, uint32_t box_rows)
+{
+    EncodeTiledFn enc = encode_fn();
+    if (!enc || rows == 0) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 4};
+    const cuuint32_t box[2] = {32, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+           CUDA_SUCCESS;
+}
+
 template <int STAGES>
 cudaError_t launch_pair(const HeadArgs &a, const CUtensorMap &ma, int tiles_m, int sms,
                         cudaStream_t stream)
@@ -688,7 +763,8 @@ cudaError_t launch_pair(const HeadArgs &a, const CUtensorMap &ma, int tiles_m, i
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    const size_t smem = (size_t)STAGES * (kBM + 128) * kBK * 2 + 1024 + 512;
+    // stages, 4 KB of output staging per epilogue warp, barriers, alignment
+    const size_t smem = (size_t)STAGES * (kBM + 128) * kBK * 2 + (kEpiThreads / 32) * 4096 + 1024 + 512;
     if (dev < 64 && !attr[dev]) {
         e = cudaFuncSetAttribute(head_tc2_kernel<STAGES>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -719,9 +795,14 @@ cudaError_t launch_pair(const HeadArgs &a, const CUtensorMap &ma, int tiles_m, i
     t.out = a.out;
     t.cfg = a.cfg;
     t.cfg_scale = a.cfg_scale;
+    t.out_rows = a.cfg ? a.batch / 2 : a.batch;
+    CUtensorMap mo;   // the logits, f32, 32 x 32 chunks (16 output rows with guidance)
+    if (!make_map_f32(&mo, a.out, (uint64_t)t.out_rows, (uint64_t)a.n_cb * a.vocab,
+                      a.cfg ? 16 : 32))
+        return cudaErrorInvalidValue;
     const int pairs = dev < 64 ? pairs_cap[dev] : 1;
     const int grid = 2 * (t.n_tiles < pairs ? t.n_tiles : pairs);
-    head_tc2_kernel<STAGES><<<grid, kThreads, smem, stream>>>(ma, mb, t);
+    head_tc2_kernel<STAGES><<<grid, kThreads, smem, stream>>>(ma, mb, mo, t);
     return cudaGetLastError();
 }
 
@@ -756,6 +837,7 @@ cudaError_t launch_bn(const HeadArgs &a, const CUtensorMap &ma, int tiles_m, int
     t.out = a.out;
     t.cfg = a.cfg;
     t.cfg_scale = a.cfg_scale;
+    t.out_rows = a.cfg ? a.batch / 2 : a.batch;
     const int grid = t.n_tiles < sms ? t.n_tiles : sms;
     head_tc_kernel<BN, STAGES><<<grid, kThreads, smem, stream>>>(ma, mb, t);
     return cudaGetLastError();
