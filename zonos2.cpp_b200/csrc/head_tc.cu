@@ -14,7 +14,9 @@
 //               two accumulators alternate so the epilogue of one tile
 //               overlaps the MMAs of the next;
 //   warps 2..9  epilogue: tcgen05.ld of their 32 TMEM lanes (two warps per lane
-//               quarter, each half of the columns), softcap, f32 store.
+//               quarter, each half of the columns), softcap, then each 32 x 32
+//               f32 chunk staged in the warp's 4 KB of shared memory and
+//               stored by a tensor copy (whole 128-byte row pieces).
 // Stages hand over through mbarriers: TMA completes `full`, tcgen05.commit
 // releases `empty` and signals `tfull`, the epilogue releases `tempty`.
 // Every wait is bounded: after ~2 s it records an error in g_device_error and
@@ -198,13 +200,11 @@ struct TcArgs {
     int out_rows;   // rows of out: batch, or batch / 2 with cfg
 };
 
-// The epilogue's store of one 32-column chunk of row `row` (lane = row's lane in
-// its warp; rows 2s and 2s+1 sit in lanes of one warp): the softcap, and with
-// classifier-free guidance the blend u + s * (c - u) of the pair, taken from
-// the neighbouring lane and stored by the even lane as output row s
-// (src/zonos2_generate.cpp:178-183).
-// The same chunk's 32 output values of this lane's row (every lane takes part:
-// the guidance blend reads the neighbouring lane).
+// The epilogue's 32 output values of one 32-column chunk of this lane's row
+// (rows 2s and 2s+1 sit in neighbouring lanes of one warp): the softcap, and
+// with classifier-free guidance the blend u + s * (c - u) of the pair, taken
+// from the neighbouring lane; the even lane's values are output row s
+// (src/zonos2_generate.cpp:178-183).  Every lane takes part.
 __device__ __forceinline__ void finish_chunk(const TcArgs &args, const uint32_t (&r)[32], float k2,
                                              float (&o)[32])
 {
@@ -220,35 +220,11 @@ __device__ __forceinline__ void finish_chunk(const TcArgs &args, const uint32_t 
     }
 }
 
-__device__ __forceinline__ void store_chunk(const TcArgs &args, const uint32_t (&r)[32], int row,
-                                            size_t col, float k2)
-{
-    const float cap = args.softcap;
-    const size_t ld = (size_t)(args.n_cb * args.vocab);
-    const bool even = (row & 1) == 0;
-    float *dst = args.cfg ? args.out + (size_t)(row >> 1) * ld + col
-                          : args.out + (size_t)row * ld + col;
-    const bool st = row < args.batch && (!args.cfg || even);
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-        float o[4];
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-            const float l = __uint_as_float(r[4 * i + e]);
-            o[e] = cap > 0.0f ? softcap_fast(l, cap, k2) : l;
-            if (args.cfg) {
-                const float u = __shfl_xor_sync(kFull, o[e], 1);
-                o[e] = __fadd_rn(u, __fmul_rn(args.cfg_scale, __fsub_rn(o[e], u)));
-            }
-        }
-        if (st) reinterpret_cast<float4 *>(dst)[i] = make_float4(o[0], o[1], o[2], o[3]);
-    }
-}
-
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     head_tc_kernel(const __grid_constant__ CUtensorMap map_a,
-                   const __grid_constant__ CUtensorMap map_b, const TcArgs args)
+                   const __grid_constant__ CUtensorMap map_b,
+                   const __grid_constant__ CUtensorMap map_o, const TcArgs args)
 {
     constexpr uint32_t kABytes = kBM * kBK * 2;
     constexpr uint32_t kBBytes = BN * kBK * 2;
@@ -262,7 +238,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * kStageBytes);
+    // stages, then 4 KB of output staging per epilogue warp, then the barriers
+    uint64_t *bars =
+        reinterpret_cast<uint64_t *>(smem + STAGES * kStageBytes + (kEpiThreads / 32) * 4096);
     // bars: full[STAGES], empty[STAGES], tfull[2], tempty[2]; then the TMEM slot
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 4);
     __shared__ int s_abort;
@@ -288,6 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         prefetch_map(&map_a);
         prefetch_map(&map_b);
+        prefetch_map(&map_o);
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -369,9 +348,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok) s_abort = 1;
         }
     } else {
-        // ---- epilogue: TMEM -> softcap -> global
+        // ---- epilogue: TMEM -> softcap -> global, through the warp's staging
+        // buffer and tensor stores as in the two-SM kernel below
         const int q = warp & 3;   // the TMEM lane quarter this warp may read
         const int half = (warp - 2) >> 2;   // which half of the tile's columns
+        const uint32_t stage_o = smem_u32(smem + STAGES * kStageBytes + (warp - 2) * 4096);
+        const int orow = args.cfg ? lane >> 1 : lane;
+        const bool owner = !args.cfg || (lane & 1) == 0;
         int local = 0;
         for (int tile = blockIdx.x; tile < args.n_tiles; tile += gridDim.x, local++) {
             const int acc = local & 1;
@@ -383,17 +366,36 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (*(volatile int *)&s_abort) break;
             tc_fence_after();
             const int mt = tile % args.tiles_m, nt = tile / args.tiles_m;
-            const int row = mt * kBM + 32 * q + lane;
+            const int row0 = mt * kBM + 32 * q;
+            const int y0 = args.cfg ? row0 >> 1 : row0;
             const float k2 = 2.0f * 1.4426950408889634f / args.softcap;   // 2 log2(e) / cap
 #pragma unroll 1
             for (int ch = half * (BN / 64); ch < (half + 1) * (BN / 64); ch++) {
                 uint32_t r[32];
                 tmem_ld32(tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BN + 32 * ch), r);
-                store_chunk(args, r, row, (size_t)nt * BN + 32 * ch, k2);
+                float o[32];
+                finish_chunk(args, r, k2, o);
+                if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+                __syncwarp();
+                if (owner) {
+#pragma unroll
+                    for (int c = 0; c < 8; c++)
+                        asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(
+                                         stage_o + orow * 128 + ((c ^ (orow & 7)) << 4)),
+                                     "f"(o[4 * c]), "f"(o[4 * c + 1]), "f"(o[4 * c + 2]),
+                                     "f"(o[4 * c + 3])
+                                     : "memory");
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0 && y0 < args.out_rows)
+                    tma_store_2d(&map_o, stage_o, nt * BN + 32 * ch, y0);
             }
             tc_fence_before();
             mbar_arrive(tempty(acc));
         }
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        __syncwarp();
     }
 
     tc_fence_before();
@@ -814,7 +816,8 @@ cudaError_t launch_bn(const HeadArgs &a, const CUtensorMap &ma, int tiles_m, int
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    const size_t smem = (size_t)STAGES * (kBM + BN) * kBK * 2 + 1024 + 256;
+    // stages, 4 KB of output staging per epilogue warp, barriers, alignment
+    const size_t smem = (size_t)STAGES * (kBM + BN) * kBK * 2 + (kEpiThreads / 32) * 4096 + 1024 + 512;
     if (dev < 64 && !attr[dev]) {
         e = cudaFuncSetAttribute(head_tc_kernel<BN, STAGES>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -838,8 +841,12 @@ cudaError_t launch_bn(const HeadArgs &a, const CUtensorMap &ma, int tiles_m, int
     t.cfg = a.cfg;
     t.cfg_scale = a.cfg_scale;
     t.out_rows = a.cfg ? a.batch / 2 : a.batch;
+    CUtensorMap mo;
+    if (!make_map_f32(&mo, a.out, (uint64_t)t.out_rows, (uint64_t)a.n_cb * a.vocab,
+                      a.cfg ? 16 : 32))
+        return cudaErrorInvalidValue;
     const int grid = t.n_tiles < sms ? t.n_tiles : sms;
-    head_tc_kernel<BN, STAGES><<<grid, kThreads, smem, stream>>>(ma, mb, t);
+    head_tc_kernel<BN, STAGES><<<grid, kThreads, smem, stream>>>(ma, mb, mo, t);
     return cudaGetLastError();
 }
 
