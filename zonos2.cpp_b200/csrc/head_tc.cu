@@ -867,15 +867,36 @@ cudaError_t launch_head_tc_bf16(const HeadArgs &a, cudaStream_t stream)
     if (!make_map(&ma, a.hidden, (uint64_t)a.batch, (uint64_t)a.dim, kBM))
         return cudaErrorInvalidValue;
     const int tiles_m = (a.batch + kBM - 1) / kBM;
-    // the widest N tile that still gives every SM work
+    // Tile choice.  Two-SM pairs once each pair gets three or more 256 x 256 tiles
+    // (tensor-bound: a pair moves 128 + 128 operand rows per SM per tile).
+    // Below that the one-SM kernel, its N tile by a model of operand traffic: a
+    // tile rereads its A rows once per N tile and its B rows once per M tile, so a
+    // wave costs about (128 + BN) rows per SM and the launch ceil(tiles / SMs)
+    // waves; ties go to the wider tile.  Measured on a B200 (ms, 9 x 1024 x 2048):
+    //   rows   pairs   BN 256  BN 128  BN 64
+    //    128     -     0.0185  0.0184  0.0177
+    //    256   0.0227  0.0204  0.0191  0.0282
+    //    512   0.0237  0.0206  0.0306  0.0495
+    //   1024   0.0386  0.0369  0.0531  0.0915
+    //   2048   0.0669  0.0683    -       -
+    //   4096   0.1268  0.1305    -       -
     const int cols = a.n_cb * a.vocab;
-    // two-SM pairs once every pair has a 256 x 256 tile
-    if (a.vocab % 256 == 0 && ((tiles_m + 1) / 2) * (cols / 256) >= sms / 2)
+    if (a.vocab % 256 == 0 && ((tiles_m + 1) / 2) * (cols / 256) >= 3 * (sms / 2))
         return launch_pair<6>(a, ma, tiles_m, sms, stream);
-    if (a.vocab % 256 == 0 && tiles_m * (cols / 256) >= sms)
-        return launch_bn<256, 4>(a, ma, tiles_m, sms, stream);
-    if (a.vocab % 128 == 0 && tiles_m * (cols / 128) >= sms)
-        return launch_bn<128, 6>(a, ma, tiles_m, sms, stream);
+    auto waves = [&](int bn) { return ((long long)tiles_m * (cols / bn) + sms - 1) / sms; };
+    long long best = -1;
+    int pick = 64;
+    const int bns[3] = {256, 128, 64};
+    for (int bn : bns) {
+        if (a.vocab % bn != 0) continue;
+        const long long c = waves(bn) * (kBM + bn);
+        if (best < 0 || c < best) {
+            best = c;
+            pick = bn;
+        }
+    }
+    if (pick == 256) return launch_bn<256, 4>(a, ma, tiles_m, sms, stream);
+    if (pick == 128) return launch_bn<128, 6>(a, ma, tiles_m, sms, stream);
     return launch_bn<64, 8>(a, ma, tiles_m, sms, stream);
 }
 
