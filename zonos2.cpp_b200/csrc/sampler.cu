@@ -160,16 +160,28 @@ __device__ __forceinline__ float prologue(float x, int i, uint32_t seenm, uint32
     return (fin && ((allowm >> i) & 1u)) ? __fmul_rn(x, f) : -INFINITY;
 }
 
-// Gap bucket of a logit: t = min(fma(-v, 1/width, max/width), 126), and the
-// bucket is round(t), read from the low byte of t + 2^23 (the histogram does
-// this two slots at a time); -inf lands in 126, the open-ended last bucket.
-// gap_q15 is the same coordinate t + 1/2 in [0, 126.5] rounded to a multiple of
-// 2^-15: an integer below 2^22, monotone non-increasing in v.
-__device__ __forceinline__ uint32_t gap_q15(float v, float sc, float Msc, uint32_t *bucket)
+// Gap bucket of a logit: u = sat(fma(-v, s, max * s)) in [0, 1] with
+// s = 1 / (126 * width), and the bucket is round(126 u), read from the low byte
+// of 126 u + 2^23 (the histogram does this two slots at a time); -inf and gaps
+// past 126 widths land in 126, the open-ended last bucket.  The saturating fma
+// clamps on the fma pipe.  gap_q15 is the same coordinate 126 u + 1/2 rounded
+// to a multiple of 2^-15: an integer below 2^22, monotone non-increasing in v.
+__device__ __forceinline__ uint32_t gap_q15(float v, float s126, float Ms126, uint32_t *bucket)
 {
-    const float t = fminf(__fmaf_rn(-v, sc, Msc), (float)(kBuckets - 2));
-    *bucket = __float_as_uint(__fadd_rn(t, 0x1p23f)) & 0xffu;   // as the histogram's
-    return __float_as_uint(__fmaf_rn(t, 32768.0f, 16384.0f + 0x1p23f)) - 0x4B000000u;
+    float u;
+    asm("fma.rn.sat.f32 %0, %1, %2, %3;" : "=f"(u) : "f"(-v), "f"(s126), "f"(Ms126));
+    *bucket = __float_as_uint(__fmaf_rn(u, 126.0f, 0x1p23f)) & 0xffu;   // as the histogram's
+    return __float_as_uint(__fmaf_rn(u, 126.0f * 32768.0f, 16384.0f + 0x1p23f)) - 0x4B000000u;
+}
+
+// a * b + c on both halves, each saturated to [0, 1] (the packed f32x2 fma has
+// no saturating form, so two scalar ones: still the fma pipe, not the ALU's)
+__device__ __forceinline__ float2 ffma2_sat(float2 a, float2 b, float2 c)
+{
+    float2 d;
+    asm("fma.rn.sat.f32 %0, %1, %2, %3;" : "=f"(d.x) : "f"(a.x), "f"(b.x), "f"(c.x));
+    asm("fma.rn.sat.f32 %0, %1, %2, %3;" : "=f"(d.y) : "f"(a.y), "f"(b.y), "f"(c.y));
+    return d;
 }
 
 // Bit e of the result is set iff byte e of pk is <= bc (bytes and bc < 128).
@@ -1141,22 +1153,24 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
             float sc;   // any positive scale will do: every bucket below is computed from it
             asm("rcp.approx.f32 %0, %1;" : "=f"(sc) : "f"(bw));
             const float Msc = M * sc;
+            const float s126 = sc * (1.0f / (float)(kBuckets - 2));
+            const float Ms126 = M * s126;
             reinterpret_cast<uint4 *>(hist)[lane] = make_uint4(0u, 0u, 0u, 0u);
             __syncwarp();
             // bucket_bits = 0x4B000000 + b, so (bits * 4 + hbase) mod 2^32 is the
             // shared address of counter b
             const uint32_t hbase = smem_u32(hist) - 0x2C000000u;
-            const float2 nsc2 = make_float2(-sc, -sc), msc2 = make_float2(Msc, Msc);
+            const float2 ns2 = make_float2(-s126, -s126), ms2 = make_float2(Ms126, Ms126);
+            const float2 k2 = make_float2((float)(kBuckets - 2), (float)(kBuckets - 2));
             const float2 mag2 = make_float2(0x1p23f, 0x1p23f);
 #pragma unroll
             for (int j = 0; j < 8; j++) {
                 uint32_t bb[4];
 #pragma unroll
                 for (int e = 0; e < 4; e += 2) {   // bucket_bits of two slots at once
-                    float2 t = __ffma2_rn(make_float2(v[4 * j + e], v[4 * j + e + 1]), nsc2, msc2);
-                    t.x = fminf(t.x, (float)(kBuckets - 2));
-                    t.y = fminf(t.y, (float)(kBuckets - 2));
-                    t = __fadd2_rn(t, mag2);
+                    const float2 u =
+                        ffma2_sat(make_float2(v[4 * j + e], v[4 * j + e + 1]), ns2, ms2);
+                    const float2 t = __ffma2_rn(u, k2, mag2);
                     bb[e] = __float_as_uint(t.x);
                     bb[e + 1] = __float_as_uint(t.y);
                 }
@@ -1261,7 +1275,7 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
                         sm &= sm - 1u;
                         const int t = slot_token(lane, i);
                         uint32_t b8;
-                        const uint32_t q = gap_q15(rowf[t], sc, Msc, &b8);
+                        const uint32_t q = gap_q15(rowf[t], s126, Ms126, &b8);
                         int pos = kRegSortMax;
                         if (has) pos = (int)atomicAdd(hist + b8, 1u);
                         stage[pos] = ~((q << 10) | (uint32_t)t);
