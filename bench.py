@@ -64,8 +64,9 @@ DESIGN_ROW_BYTES = 4 * VOCAB + 128 + 8 + 8 + 8 + 128 / NCB + 64 / NCB
 # --no-head`, launch 11 (dram__bytes_read.sum 167.03 MB +
 # dram__bytes_write.sum 6.09 MB).
 SAMPLER_TRAFFIC_BYTES = 173.12e6
-# Kernels of ours per decode step: the uniform draw and the persistent sampler.
-LAUNCHES_PER_STEP = 2
+# Kernels of ours per decode step: the persistent sampler (the decode context
+# draws each step's uniforms during the step before).
+LAUNCHES_PER_STEP = 1
 
 
 def dist_env():
@@ -455,7 +456,7 @@ def run_ours(args):
                    "l2": "inputs larger than L2 (151 MB logits + 151 MB history per GPU per step)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": args.traffic,
-                     "kernel": "sample_rows_kernel (+ draw_uniforms_kernel)",
+                     "kernel": "sample_rows_kernel",
                      "kernel_ms": kern_ms,
                      "bytes_per_launch": launch_bytes, "peak_source": peak_src,
                      "design_bytes_per_launch": DESIGN_ROW_BYTES * rows,

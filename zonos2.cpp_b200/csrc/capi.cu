@@ -76,7 +76,8 @@ int launch_rows(const float *logits, int n_streams, int n_cb, int vocab, long lo
                 int hist_len, int hist_pos, const uint32_t *allow, int delay_step,
                 int32_t *codes, int32_t *flags, cudaStream_t stream,
                 uint16_t *counts = nullptr, uint32_t *presence = nullptr,
-                bool allow_lane_major = false)
+                bool allow_lane_major = false, const float *u_cur = nullptr,
+                float *u_next = nullptr, uint64_t *rng_ahead = nullptr)
 {
     z2::SampleArgs a{};
     a.logits = logits;
@@ -99,6 +100,9 @@ int launch_rows(const float *logits, int n_streams, int n_cb, int vocab, long lo
     a.vec_hist = hist_len > 0 && (hist_len % 4 == 0) && ((uintptr_t)hist % 16 == 0);
     a.counts = hist_len > 0 ? counts : nullptr;
     a.presence = hist_len > 0 ? presence : nullptr;
+    a.u_cur = u_cur;
+    a.u_next = u_next;
+    a.rng_ahead = rng_ahead;
     Z2_CK(z2::launch_sample(a, stream));
     return ZONOS2CU_OK;
 }
@@ -305,6 +309,12 @@ struct zonos2cu_ctx {
     int hist_pos = 0;
     uint16_t *counts = nullptr;  // [S][C][1024] occurrences of each token in the ring
     uint32_t *presence = nullptr;// [S][C][32] tokens with a nonzero count, lane-major
+    // Uniforms drawn one step ahead: u_ahead[ahead_par] holds the next step's,
+    // rng_ahead the generators after them (rng stays the state after the steps taken).
+    float *u_ahead = nullptr;    // [2][S][C]
+    uint64_t *rng_ahead = nullptr;
+    bool ahead_valid = false;    // u_ahead[ahead_par] and rng_ahead follow from rng
+    int ahead_par = 0;
     uint32_t *allow = nullptr;   // [S][32] lane-major (word l, bit 4j+e: token 4(l+32j)+e)
     bool allow_on = false;
     void *head = nullptr;        // [C*V][D] of head_dtype
@@ -401,6 +411,8 @@ int zonos2cu_ctx_create(int device, const zonos2cu_dims *d, zonos2cu_ctx **out)
         const size_t S = (size_t)d->n_streams;
         if (S == 0) break;
         e = cudaMalloc(&c->rng, sizeof(uint64_t) * 4 * S);
+        if (e == cudaSuccess) e = cudaMalloc(&c->rng_ahead, sizeof(uint64_t) * 4 * S);
+        if (e == cudaSuccess) e = cudaMalloc(&c->u_ahead, sizeof(float) * 2 * S * d->n_cb);
         if (e != cudaSuccess) { rc = cuda_fail(e, "rng"); break; }
         uint64_t *h = new (std::nothrow) uint64_t[4 * S];
         if (!h) { rc = ZONOS2CU_ENOMEM; break; }
@@ -439,6 +451,8 @@ int zonos2cu_ctx_destroy(zonos2cu_ctx *c)
     DeviceGuard g(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
     cudaFree(c->rng);
+    cudaFree(c->rng_ahead);
+    cudaFree(c->u_ahead);
     cudaFree(c->hist);
     cudaFree(c->counts);
     cudaFree(c->presence);
@@ -524,6 +538,7 @@ int zonos2cu_set_rng(zonos2cu_ctx *c, const uint64_t *state_host)
         Z2_CK(cudaMemcpyAsync(c->rng, state_host, sizeof(uint64_t) * 4 * c->dims.n_streams,
                               cudaMemcpyHostToDevice, c->stream));
     Z2_CK(cudaStreamSynchronize(c->stream));
+    c->ahead_valid = false;   // the next step draws from the new state
     return ZONOS2CU_OK;
 }
 
@@ -736,11 +751,22 @@ int zonos2cu_ctx_sample(zonos2cu_ctx *c, const float *logits_dev, long long row_
                         d.hist_len, c->hist_pos, codes_dev);
     if (rc) return rc;
     if ((rc = check_params(params, d.vocab))) return rc;
+    const size_t rows = (size_t)d.n_streams * d.n_cb;
+    if (!c->ahead_valid && d.n_streams) {   // this step's uniforms, once
+        Z2_CK(z2::launch_draw_ahead(c->rng, c->rng_ahead, d.n_streams, d.n_cb,
+                                    c->u_ahead + rows * c->ahead_par, (cudaStream_t)stream));
+        c->ahead_valid = true;
+    }
     rc = launch_rows(logits_dev, d.n_streams, d.n_cb, d.vocab, row_stride, params, c->rng,
                      c->hist, d.hist_len, c->hist_pos, c->allow_on ? c->allow : nullptr,
                      delay_step, codes_dev, flags_dev, (cudaStream_t)stream, c->counts,
-                     c->presence, /*allow_lane_major*/ true);
-    if (rc) return rc;
+                     c->presence, /*allow_lane_major*/ true, c->u_ahead + rows * c->ahead_par,
+                     c->u_ahead + rows * (c->ahead_par ^ 1), c->rng_ahead);
+    if (rc) {
+        c->ahead_valid = false;
+        return rc;
+    }
+    c->ahead_par ^= 1;
     if (c->gen_on)   // the generation loop keeps this step's frame
         Z2_CK(z2::launch_gen_append(codes_dev, d.n_streams, d.n_cb, d.vocab, c->gen_eoa,
                                     c->gen_text_pad, c->gen_max_frames, c->gen_frames,

@@ -6,15 +6,22 @@
 // forcing, non-finite guard), with the row's uniform drawn from a per-stream
 // Xoshiro256** in codebook order (src/zonos2_generate.cpp:259-267).
 //
-// Two launches per step.  draw_uniforms_kernel (one thread per stream) draws
-// the stream's n_cb uniforms in codebook order, advances its generator and
-// parks each uniform in the row's code slot.  sample_rows_kernel is persistent:
-// every warp walks rows r, r + W, r + 2W, ... (W warps in the grid) on its own,
-// so no warp waits for another; it starts under programmatic dependent launch
-// and waits for the draw grid only before it first reads a uniform.
+// sample_rows_kernel is persistent: one CTA of 28 warps per SM, whose warps
+// take the SM's rows from a shared counter; no warp waits for another.  The
+// uniforms come one of two ways:
+//  - the decode context draws them one step ahead: warp 0 of each CTA draws the
+//    next step's uniforms for a slice of streams, so a step is one launch (the
+//    first step after the generators are set is preceded by draw_ahead_kernel);
+//    the kernel runs under programmatic dependent launch and waits for the grid
+//    before it at its start, so only its launch overlaps that grid's tail;
+//  - otherwise draw_uniforms_kernel (one thread per stream) draws the stream's
+//    n_cb uniforms in codebook order, advances its generator and parks each
+//    uniform in the row's code slot, and the sampler, launched behind it under
+//    programmatic dependent launch, waits for it only before it first reads a
+//    uniform.
 //
 // Per row: one bulk copy (TMA) lands the logits in the warp's shared memory
-// and the row a stride ahead is prefetched into L2.  Lane l holds slots
+// while the warp finishes its previous row.  Lane l holds slots
 // 4*(l + 32*j) + e, j < 8, e < 4, so every access is a conflict-free 128-bit
 // one, and a lane-major bitmap (word l, bit 4*j + e) gives a lane all its mask
 // bits in one load; the decode context keeps its history set and allow mask in
@@ -544,6 +551,45 @@ __global__ void __launch_bounds__(128) draw_uniforms_kernel(uint64_t *rng, int n
     sp[1] = make_ulonglong2(g.s2, g.s3);
 }
 
+// One stream's n_cb uniforms in codebook order from rng_in into u; the advanced
+// state goes to rng_out.
+__device__ __forceinline__ void draw_stream(const uint64_t *rng_in, uint64_t *rng_out, int s,
+                                            int n_cb, float *u)
+{
+    const ulonglong2 *sp = reinterpret_cast<const ulonglong2 *>(rng_in + 4 * (size_t)s);
+    const ulonglong2 st01 = sp[0], st23 = sp[1];
+    Xo256 g{st01.x, st01.y, st23.x, st23.y};
+    for (int c = 0; c < n_cb; c++) u[(size_t)s * n_cb + c] = g.randf();
+    ulonglong2 *op = reinterpret_cast<ulonglong2 *>(rng_out + 4 * (size_t)s);
+    op[0] = make_ulonglong2(g.s0, g.s1);
+    op[1] = make_ulonglong2(g.s2, g.s3);
+}
+
+// Warp 0 of each sampler CTA, when the uniforms run one step ahead: for the
+// CTA's slice of streams, the state after this step's draws becomes the
+// stream's state, and the next step's uniforms are drawn from it.
+__device__ __noinline__ void draw_ahead_slice(uint64_t *rng, uint64_t *rng_ahead, float *u_next,
+                                              int n_streams, int n_cb, int lane)
+{
+    const int per = (n_streams + gridDim.x - 1) / gridDim.x;
+    const int s_end = min(n_streams, (int)blockIdx.x * per + per);
+    for (int s = (int)blockIdx.x * per + lane; s < s_end; s += 32) {
+        const ulonglong2 *ap = reinterpret_cast<const ulonglong2 *>(rng_ahead + 4 * (size_t)s);
+        ulonglong2 *cp = reinterpret_cast<ulonglong2 *>(rng + 4 * (size_t)s);
+        const ulonglong2 st01 = ap[0], st23 = ap[1];
+        cp[0] = st01;
+        cp[1] = st23;
+        draw_stream(rng_ahead, rng_ahead, s, n_cb, u_next);
+    }
+}
+
+__global__ void __launch_bounds__(128) draw_ahead_kernel(const uint64_t *rng_in, uint64_t *rng_out,
+                                                         int n_streams, int n_cb, float *u)
+{
+    const int s = blockIdx.x * 128 + threadIdx.x;
+    if (s < n_streams) draw_stream(rng_in, rng_out, s, n_cb, u);
+}
+
 // Descending bitonic sort of 128 keys held four per lane (key e of lane l is
 // element 4*l + e): compare-exchanges inside a lane for distances 1 and 2,
 // shuffles across lanes for the rest.
@@ -975,7 +1021,12 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
     item_at(blockIdx.x + (long long)gridDim.x * w, s, cb);
 
     uint32_t phase = 0u;
-    bool drawn = false;     // the draw grid has been waited for
+    // With uniforms drawn ahead the kernel before this one may be the previous
+    // step's sampler (history index, generators) or the head (logits): wait for it
+    // before any global read.  Either way the next launch may be scheduled now.
+    grid_dep_launch();
+    if (a.u_cur) grid_dep_wait();
+    bool drawn = a.u_cur != nullptr;   // the grid before this one has been waited for
     bool pending = false;   // the copy of the current row is in flight
     uint32_t seen_next = 0u, allow_next = ~0u;   // lane-major masks of the next row
     int ev_next = -1;   // lane 0: the token the next row's append evicts
@@ -994,6 +1045,7 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
         pending = true;
     };
     if (cb < NCB) issue(s, cb);
+    if (a.u_cur && w == 0) draw_ahead_slice(a.rng, a.rng_ahead, a.u_next, S_, NCB, lane);
 
     while (cb < NCB) {
         const long long r = (long long)s * NCB + cb;
@@ -1237,7 +1289,7 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
                 grid_dep_wait();
                 drawn = true;
             }
-            const float u = __uint_as_float(__ldcg(slots + r));
+            const float u = a.u_cur ? __ldg(a.u_cur + r) : __uint_as_float(__ldcg(slots + r));
 
             if (!topk_on || n_c > kRegSortMax) {
                 RowKnobs kn;
@@ -1503,6 +1555,15 @@ cudaError_t launch_history_index(const int32_t *hist, long long rows, int hist_l
     return cudaGetLastError();
 }
 
+cudaError_t launch_draw_ahead(const uint64_t *rng_in, uint64_t *rng_out, int n_streams, int n_cb,
+                              float *u, cudaStream_t stream)
+{
+    if (n_streams == 0) return cudaSuccess;
+    draw_ahead_kernel<<<(unsigned)((n_streams + 127) / 128), 128, 0, stream>>>(rng_in, rng_out,
+                                                                              n_streams, n_cb, u);
+    return cudaGetLastError();
+}
+
 size_t sample_smem_bytes() { return (size_t)kCtaHeader + (size_t)kWarps * kWarpStride; }
 
 namespace {
@@ -1549,10 +1610,12 @@ cudaError_t launch_sample(const SampleArgs &a, cudaStream_t stream)
     e = launch_info(dev, &cap);
     if (e != cudaSuccess) return e;
 
-    draw_uniforms_kernel<<<(unsigned)((a.n_streams + 127) / 128), 128, 0, stream>>>(
-        a.rng, a.n_streams, a.n_cb, reinterpret_cast<uint32_t *>(a.codes));
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
+    if (!a.u_cur) {
+        draw_uniforms_kernel<<<(unsigned)((a.n_streams + 127) / 128), 128, 0, stream>>>(
+            a.rng, a.n_streams, a.n_cb, reinterpret_cast<uint32_t *>(a.codes));
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
 
     // One CTA per SM, or per row when there are fewer rows than SMs: a small batch
     // spreads over as many SMs as it has rows.
@@ -1562,6 +1625,10 @@ cudaError_t launch_sample(const SampleArgs &a, cudaStream_t stream)
     cfg.blockDim = dim3(32 * kWarps);
     cfg.dynamicSmemBytes = sample_smem_bytes();
     cfg.stream = stream;
+    // Programmatic dependent launch: behind the draw kernel the rows' copies start
+    // before griddepcontrol.wait (the draw writes only the code slots); with
+    // uniforms drawn ahead the kernel waits before its first global read, and only
+    // its launch and set-up overlap the kernel before it.
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;

@@ -35,11 +35,26 @@ struct SampleArgs {
     // updates counts and bitmap for the token it evicts and the one it appends.
     uint16_t *counts;        // [n_streams][n_cb][1024] or nullptr
     uint32_t *presence;      // [n_streams][n_cb][32] lane-major, or nullptr
+    // Uniforms drawn one step ahead (the decode context).  When u_cur is set the
+    // step is one launch: row r reads its uniform from u_cur[r]; warp 0 of each
+    // CTA sets rng to rng_ahead (the state after this step's draws) for its slice
+    // of streams, draws the next step's uniforms into u_next and leaves rng_ahead
+    // the state after them.  When u_cur is nullptr a draw kernel precedes the
+    // sampler and parks the uniforms in the code slots.
+    const float *u_cur;      // [n_streams][n_cb] or nullptr
+    float *u_next;           // [n_streams][n_cb]
+    uint64_t *rng_ahead;     // [n_streams][4]
 };
 
 // Enqueues one sampling step (the uniform draw, then the persistent sampler
 // under programmatic dependent launch); returns the cudaError_t of the launches.
 cudaError_t launch_sample(const SampleArgs &a, cudaStream_t stream);
+
+// Draws one step's uniforms from rng_in into u ([n_streams][n_cb] f32) and
+// writes the advanced states to rng_out (rng_in is left as it is): the decode
+// context's first step, and the first after its generators are set.
+cudaError_t launch_draw_ahead(const uint64_t *rng_in, uint64_t *rng_out, int n_streams, int n_cb,
+                              float *u, cudaStream_t stream);
 
 // Shared memory bytes of one sampler CTA.
 size_t sample_smem_bytes();
