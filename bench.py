@@ -61,9 +61,9 @@ ROW_BYTES = 4 * VOCAB + 4 * HIST + 8 + 128 / NCB
 DESIGN_ROW_BYTES = 4 * VOCAB + 128 + 8 + 8 + 8 + 128 / NCB + 64 / NCB
 # DRAM bytes (read + write) of one sample_rows_kernel launch on this workload,
 # from an ncu capture of `bench.py --steps 12 --warmup 3 --no-cpu-baseline
-# --no-head`, launch 11 (dram__bytes_read.sum 167.03 MB +
-# dram__bytes_write.sum 6.09 MB).
-SAMPLER_TRAFFIC_BYTES = 173.12e6
+# --no-head`, launch 11 (dram__bytes_read.sum 167.17 MB +
+# dram__bytes_write.sum 7.11 MB).
+SAMPLER_TRAFFIC_BYTES = 174.28e6
 # Kernels of ours per decode step: the persistent sampler (the decode context
 # draws each step's uniforms during the step before).
 LAUNCHES_PER_STEP = 1
