@@ -502,13 +502,13 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t bar)
 // No load is multicast: every copy lands in the CTA that issued it.  A CTA that
 // gives up waits at the final cluster barrier, so its shared memory outlives
 // any copy of its own still in flight while rank 0 drains `full`.
-template <int STAGES>
+template <int BN, int STAGES>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     head_tc2_kernel(const __grid_constant__ CUtensorMap map_a,
                     const __grid_constant__ CUtensorMap map_b,
                     const __grid_constant__ CUtensorMap map_o, const TcArgs args)
 {
-    constexpr int BN = 256;                    // N of the pair's tile; each CTA holds 128 B rows
+    // BN: N of the pair's tile (256 or 128); each CTA holds BN / 2 of its B rows
     constexpr uint32_t kABytes = kBM * kBK * 2;
     constexpr uint32_t kBBytes = (BN / 2) * kBK * 2;
     constexpr uint32_t kStageBytes = kABytes + kBBytes;
@@ -756,7 +756,7 @@ bool make_map_f32(CUtensorMap *m, void *base, uint64_t rows, uint64_t cols, uint
            CUDA_SUCCESS;
 }
 
-template <int STAGES>
+template <int BN, int STAGES>
 cudaError_t launch_pair(const HeadArgs &a, const CUtensorMap &ma, int tiles_m, int sms,
                         cudaStream_t stream)
 {
@@ -766,9 +766,10 @@ cudaError_t launch_pair(const HeadArgs &a, const CUtensorMap &ma, int tiles_m, i
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     // stages, 4 KB of output staging per epilogue warp, barriers, alignment
-    const size_t smem = (size_t)STAGES * (kBM + 128) * kBK * 2 + (kEpiThreads / 32) * 4096 + 1024 + 512;
+    const size_t smem =
+        (size_t)STAGES * (kBM + BN / 2) * kBK * 2 + (kEpiThreads / 32) * 4096 + 1024 + 512;
     if (dev < 64 && !attr[dev]) {
-        e = cudaFuncSetAttribute(head_tc2_kernel<STAGES>,
+        e = cudaFuncSetAttribute(head_tc2_kernel<BN, STAGES>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
         cudaLaunchConfig_t cfg = {};
@@ -776,13 +777,13 @@ cudaError_t launch_pair(const HeadArgs &a, const CUtensorMap &ma, int tiles_m, i
         cfg.blockDim = dim3(kThreads);
         cfg.dynamicSmemBytes = smem;
         int n = 0;
-        e = cudaOccupancyMaxActiveClusters(&n, head_tc2_kernel<STAGES>, &cfg);
+        e = cudaOccupancyMaxActiveClusters(&n, head_tc2_kernel<BN, STAGES>, &cfg);
         if (e != cudaSuccess) return e;
         pairs_cap[dev] = n > 0 ? n : 1;
         attr[dev] = true;
     }
-    CUtensorMap mb;   // each CTA of a pair loads 128 of the tile's 256 weight rows
-    if (!make_map(&mb, a.W, (uint64_t)a.n_cb * a.rows_per_cb, (uint64_t)a.dim, 128))
+    CUtensorMap mb;   // each CTA of a pair loads half of the tile's BN weight rows
+    if (!make_map(&mb, a.W, (uint64_t)a.n_cb * a.rows_per_cb, (uint64_t)a.dim, BN / 2))
         return cudaErrorInvalidValue;
     TcArgs t;
     t.batch = a.batch;
@@ -791,7 +792,7 @@ cudaError_t launch_pair(const HeadArgs &a, const CUtensorMap &ma, int tiles_m, i
     t.rows_per_cb = a.rows_per_cb;
     t.dim = a.dim;
     t.tiles_m = tiles_m;
-    t.tiles_n = a.n_cb * (a.vocab / 256);
+    t.tiles_n = a.n_cb * (a.vocab / BN);
     t.n_tiles = ((tiles_m + 1) / 2) * t.tiles_n;
     t.softcap = a.softcap;
     t.out = a.out;
@@ -804,7 +805,7 @@ cudaError_t launch_pair(const HeadArgs &a, const CUtensorMap &ma, int tiles_m, i
         return cudaErrorInvalidValue;
     const int pairs = dev < 64 ? pairs_cap[dev] : 1;
     const int grid = 2 * (t.n_tiles < pairs ? t.n_tiles : pairs);
-    head_tc2_kernel<STAGES><<<grid, kThreads, smem, stream>>>(ma, mb, mo, t);
+    head_tc2_kernel<BN, STAGES><<<grid, kThreads, smem, stream>>>(ma, mb, mo, t);
     return cudaGetLastError();
 }
 
@@ -880,16 +881,18 @@ cudaError_t launch_head_tc_bf16(const HeadArgs &a, cudaStream_t stream)
     //   1024   0.0386  0.0369  0.0531  0.0915
     //   2048   0.0669  0.0683    -       -
     //   4096   0.1268  0.1305    -       -
+    // Pairs with 128-wide tiles (128 + 64 rows per SM) measured slower still:
+    // 0.0217 ms at 256 rows, 0.0354 at 512, 0.0592 at 1024.
     const int cols = a.n_cb * a.vocab;
     if (a.vocab % 256 == 0 && ((tiles_m + 1) / 2) * (cols / 256) >= 3 * (sms / 2))
-        return launch_pair<6>(a, ma, tiles_m, sms, stream);
-    auto waves = [&](int bn) { return ((long long)tiles_m * (cols / bn) + sms - 1) / sms; };
+        return launch_pair<256, 6>(a, ma, tiles_m, sms, stream);
+    auto waves = [&](long long tiles, int slots) { return (tiles + slots - 1) / slots; };
     long long best = -1;
     int pick = 64;
     const int bns[3] = {256, 128, 64};
     for (int bn : bns) {
         if (a.vocab % bn != 0) continue;
-        const long long c = waves(bn) * (kBM + bn);
+        const long long c = waves((long long)tiles_m * (cols / bn), sms) * (kBM + bn);
         if (best < 0 || c < best) {
             best = c;
             pick = bn;
