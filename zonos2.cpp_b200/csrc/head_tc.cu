@@ -245,6 +245,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 4);
     __shared__ int s_abort;
 
+    // the next kernel (the sampler) may be scheduled as SMs free up; it waits for
+    // this grid before it reads anything
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int KB = args.dim / kBK;
     auto full = [&](int s) { return smem_u32(bars + s); };
@@ -279,6 +282,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Launched under programmatic dependent launch: the set-up above overlaps the
+    // kernel before this one; nothing global is read or written before it ends.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 
     if (warp == 0) {
         // ---- TMA producer
@@ -526,6 +532,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 4);
     __shared__ int s_abort;
 
+    // the next kernel (the sampler) may be scheduled as SMs free up; it waits for
+    // this grid before it reads anything
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_rank();
     const int KB = args.dim / kBK;
@@ -562,6 +571,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     cluster_sync();    // barriers of both CTAs initialised before any remote arrive
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Launched under programmatic dependent launch: the set-up above overlaps the
+    // kernel before this one; nothing global is read or written before it ends.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 
     const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
     const int tiles_m2 = (args.tiles_m + 1) >> 1;   // 256-row blocks
@@ -756,6 +768,26 @@ bool make_map_f32(CUtensorMap *m, void *base, uint64_t rows, uint64_t cols, uint
            CUDA_SUCCESS;
 }
 
+// Launches a head kernel under programmatic dependent launch (its set-up overlaps
+// the previous kernel's tail; it waits for that grid before any global access).
+template <class Kernel>
+cudaError_t launch_pdl(Kernel kernel, int grid, size_t smem, cudaStream_t stream,
+                       const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mo,
+                       const TcArgs &t)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, ma, mb, mo, t);
+}
+
 template <int BN, int STAGES>
 cudaError_t launch_pair(const HeadArgs &a, const CUtensorMap &ma, int tiles_m, int sms,
                         cudaStream_t stream)
@@ -805,8 +837,7 @@ cudaError_t launch_pair(const HeadArgs &a, const CUtensorMap &ma, int tiles_m, i
         return cudaErrorInvalidValue;
     const int pairs = dev < 64 ? pairs_cap[dev] : 1;
     const int grid = 2 * (t.n_tiles < pairs ? t.n_tiles : pairs);
-    head_tc2_kernel<BN, STAGES><<<grid, kThreads, smem, stream>>>(ma, mb, mo, t);
-    return cudaGetLastError();
+    return launch_pdl(head_tc2_kernel<BN, STAGES>, grid, smem, stream, ma, mb, mo, t);
 }
 
 template <int BN, int STAGES>
@@ -847,8 +878,7 @@ cudaError_t launch_bn(const HeadArgs &a, const CUtensorMap &ma, int tiles_m, int
                       a.cfg ? 16 : 32))
         return cudaErrorInvalidValue;
     const int grid = t.n_tiles < sms ? t.n_tiles : sms;
-    head_tc_kernel<BN, STAGES><<<grid, kThreads, smem, stream>>>(ma, mb, mo, t);
-    return cudaGetLastError();
+    return launch_pdl(head_tc_kernel<BN, STAGES>, grid, smem, stream, ma, mb, mo, t);
 }
 
 }  // namespace
