@@ -220,7 +220,7 @@ __device__ __forceinline__ void finish_chunk(const TcArgs &args, const uint32_t 
     }
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int KSUB>
 __global__ void __launch_bounds__(kThreads, 1)
     head_tc_kernel(const __grid_constant__ CUtensorMap map_a,
                    const __grid_constant__ CUtensorMap map_b,
@@ -228,7 +228,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 {
     constexpr uint32_t kABytes = kBM * kBK * 2;
     constexpr uint32_t kBBytes = BN * kBK * 2;
-    constexpr uint32_t kStageBytes = kABytes + kBBytes;
+    constexpr uint32_t kSubBytes = kABytes + kBBytes;   // one 64-deep K slice of A and B
+    constexpr uint32_t kStageBytes = KSUB * kSubBytes;    // KSUB slices per stage
     constexpr uint32_t kTmemCols = 2 * BN;
     // tcgen05 kind::f16 instruction descriptor: D f32, A and B bf16, both
     // K-major, N = BN, M = 128.
@@ -249,7 +250,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // this grid before it reads anything
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int KB = args.dim / kBK;
+    const int KB = args.dim / (kBK * KSUB);
     auto full = [&](int s) { return smem_u32(bars + s); };
     auto empty = [&](int s) { return smem_u32(bars + STAGES + s); };
     auto tfull = [&](int a) { return smem_u32(bars + 2 * STAGES + a); };
@@ -306,8 +307,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     const uint32_t sa = smem_u32(smem + s * kStageBytes);
                     mbar_expect_tx(full(s), kStageBytes);
-                    tma_load_2d(sa, &map_a, kb * kBK, a_row, full(s));
-                    tma_load_2d(sa + kABytes, &map_b, kb * kBK, b_row, full(s));
+#pragma unroll
+                    for (int j = 0; j < KSUB; j++) {
+                        const int kx = (kb * KSUB + j) * kBK;
+                        tma_load_2d(sa + j * kSubBytes, &map_a, kx, a_row, full(s));
+                        tma_load_2d(sa + j * kSubBytes + kABytes, &map_b, kx, b_row, full(s));
+                    }
                 }
             }
             if (!ok) {
@@ -342,11 +347,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     tc_fence_after();
                     const uint32_t sa = smem_u32(smem + s * kStageBytes);
-                    const uint64_t ad = sw128_desc(sa), bd = sw128_desc(sa + kABytes);
 #pragma unroll
-                    for (int k = 0; k < kBK / 16; k++)   // 32 bytes of K per instruction
-                        mma_bf16(d_tmem, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), kIdesc,
-                                 (kb | k) != 0);
+                    for (int j = 0; j < KSUB; j++) {
+                        const uint64_t ad = sw128_desc(sa + j * kSubBytes);
+                        const uint64_t bd = sw128_desc(sa + j * kSubBytes + kABytes);
+#pragma unroll
+                        for (int k = 0; k < kBK / 16; k++)   // 32 bytes of K per instruction
+                            mma_bf16(d_tmem, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), kIdesc,
+                                     (kb | j | k) != 0);
+                    }
                     mma_commit(empty(s));
                 }
                 if (ok) mma_commit(tfull(acc));
@@ -508,7 +517,7 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t bar)
 // No load is multicast: every copy lands in the CTA that issued it.  A CTA that
 // gives up waits at the final cluster barrier, so its shared memory outlives
 // any copy of its own still in flight while rank 0 drains `full`.
-template <int BN, int STAGES>
+template <int BN, int STAGES, int KSUB>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     head_tc2_kernel(const __grid_constant__ CUtensorMap map_a,
                     const __grid_constant__ CUtensorMap map_b,
@@ -517,7 +526,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // BN: N of the pair's tile (256 or 128); each CTA holds BN / 2 of its B rows
     constexpr uint32_t kABytes = kBM * kBK * 2;
     constexpr uint32_t kBBytes = (BN / 2) * kBK * 2;
-    constexpr uint32_t kStageBytes = kABytes + kBBytes;
+    constexpr uint32_t kSubBytes = kABytes + kBBytes;   // one 64-deep K slice of A and B
+    constexpr uint32_t kStageBytes = KSUB * kSubBytes;    // KSUB slices per stage
     constexpr uint32_t kTmemCols = 2 * BN;
     constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
                                 ((uint32_t)((2 * kBM) >> 4) << 24);
@@ -537,7 +547,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_rank();
-    const int KB = args.dim / kBK;
+    const int KB = args.dim / (kBK * KSUB);
     auto full = [&](int s) { return smem_u32(bars + s); };
     auto empty = [&](int s) { return smem_u32(bars + STAGES + s); };
     auto tfull = [&](int a) { return smem_u32(bars + 2 * STAGES + a); };
@@ -600,8 +610,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     const uint32_t sa = smem_u32(smem + s * kStageBytes);
                     if (rank == 0) mbar_expect_tx(full(s), 2 * kStageBytes);   // both halves
                     const uint32_t fb = peer_addr(full(s), 0);   // rank 0's, as a cluster address
-                    tma_load_2d_pair(sa, &map_a, kb * kBK, a_row, fb);
-                    tma_load_2d_pair(sa + kABytes, &map_b, kb * kBK, b_row, fb);
+#pragma unroll
+                    for (int j = 0; j < KSUB; j++) {
+                        const int kx = (kb * KSUB + j) * kBK;
+                        tma_load_2d_pair(sa + j * kSubBytes, &map_a, kx, a_row, fb);
+                        tma_load_2d_pair(sa + j * kSubBytes + kABytes, &map_b, kx, b_row, fb);
+                    }
                 }
             }
             if (!ok) {
@@ -636,11 +650,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     }
                     tc_fence_after();
                     const uint32_t sa = smem_u32(smem + s * kStageBytes);
-                    const uint64_t ad = sw128_desc(sa), bd = sw128_desc(sa + kABytes);
 #pragma unroll
-                    for (int k = 0; k < kBK / 16; k++)
-                        mma_bf16_pair(d_tmem, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), kIdesc,
-                                      (kb | k) != 0);
+                    for (int j = 0; j < KSUB; j++) {
+                        const uint64_t ad = sw128_desc(sa + j * kSubBytes);
+                        const uint64_t bd = sw128_desc(sa + j * kSubBytes + kABytes);
+#pragma unroll
+                        for (int k = 0; k < kBK / 16; k++)
+                            mma_bf16_pair(d_tmem, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k),
+                                          kIdesc, (kb | j | k) != 0);
+                    }
                     mma_commit_pair(empty(s));
                     mma_commit_pair(peer_addr(empty(s), 1));
                 }
@@ -788,7 +806,7 @@ cudaError_t launch_pdl(Kernel kernel, int grid, size_t smem, cudaStream_t stream
     return cudaLaunchKernelEx(&cfg, kernel, ma, mb, mo, t);
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int KSUB>
 cudaError_t launch_pair(const HeadArgs &a, const CUtensorMap &ma, int tiles_m, int sms,
                         cudaStream_t stream)
 {
@@ -799,9 +817,9 @@ cudaError_t launch_pair(const HeadArgs &a, const CUtensorMap &ma, int tiles_m, i
     if (e != cudaSuccess) return e;
     // stages, 4 KB of output staging per epilogue warp, barriers, alignment
     const size_t smem =
-        (size_t)STAGES * (kBM + BN / 2) * kBK * 2 + (kEpiThreads / 32) * 4096 + 1024 + 512;
+        (size_t)STAGES * KSUB * (kBM + BN / 2) * kBK * 2 + (kEpiThreads / 32) * 4096 + 1024 + 512;
     if (dev < 64 && !attr[dev]) {
-        e = cudaFuncSetAttribute(head_tc2_kernel<BN, STAGES>,
+        e = cudaFuncSetAttribute(head_tc2_kernel<BN, STAGES, KSUB>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
         cudaLaunchConfig_t cfg = {};
@@ -809,7 +827,7 @@ cudaError_t launch_pair(const HeadArgs &a, const CUtensorMap &ma, int tiles_m, i
         cfg.blockDim = dim3(kThreads);
         cfg.dynamicSmemBytes = smem;
         int n = 0;
-        e = cudaOccupancyMaxActiveClusters(&n, head_tc2_kernel<BN, STAGES>, &cfg);
+        e = cudaOccupancyMaxActiveClusters(&n, head_tc2_kernel<BN, STAGES, KSUB>, &cfg);
         if (e != cudaSuccess) return e;
         pairs_cap[dev] = n > 0 ? n : 1;
         attr[dev] = true;
@@ -837,10 +855,10 @@ cudaError_t launch_pair(const HeadArgs &a, const CUtensorMap &ma, int tiles_m, i
         return cudaErrorInvalidValue;
     const int pairs = dev < 64 ? pairs_cap[dev] : 1;
     const int grid = 2 * (t.n_tiles < pairs ? t.n_tiles : pairs);
-    return launch_pdl(head_tc2_kernel<BN, STAGES>, grid, smem, stream, ma, mb, mo, t);
+    return launch_pdl(head_tc2_kernel<BN, STAGES, KSUB>, grid, smem, stream, ma, mb, mo, t);
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int KSUB>
 cudaError_t launch_bn(const HeadArgs &a, const CUtensorMap &ma, int tiles_m, int sms,
                       cudaStream_t stream)
 {
@@ -849,9 +867,10 @@ cudaError_t launch_bn(const HeadArgs &a, const CUtensorMap &ma, int tiles_m, int
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     // stages, 4 KB of output staging per epilogue warp, barriers, alignment
-    const size_t smem = (size_t)STAGES * (kBM + BN) * kBK * 2 + (kEpiThreads / 32) * 4096 + 1024 + 512;
+    const size_t smem =
+        (size_t)STAGES * KSUB * (kBM + BN) * kBK * 2 + (kEpiThreads / 32) * 4096 + 1024 + 512;
     if (dev < 64 && !attr[dev]) {
-        e = cudaFuncSetAttribute(head_tc_kernel<BN, STAGES>,
+        e = cudaFuncSetAttribute(head_tc_kernel<BN, STAGES, KSUB>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
         attr[dev] = true;
@@ -878,7 +897,7 @@ cudaError_t launch_bn(const HeadArgs &a, const CUtensorMap &ma, int tiles_m, int
                       a.cfg ? 16 : 32))
         return cudaErrorInvalidValue;
     const int grid = t.n_tiles < sms ? t.n_tiles : sms;
-    return launch_pdl(head_tc_kernel<BN, STAGES>, grid, smem, stream, ma, mb, mo, t);
+    return launch_pdl(head_tc_kernel<BN, STAGES, KSUB>, grid, smem, stream, ma, mb, mo, t);
 }
 
 }  // namespace
@@ -914,8 +933,12 @@ cudaError_t launch_head_tc_bf16(const HeadArgs &a, cudaStream_t stream)
     // Pairs with 128-wide tiles (128 + 64 rows per SM) measured slower still:
     // 0.0217 ms at 256 rows, 0.0354 at 512, 0.0592 at 1024.
     const int cols = a.n_cb * a.vocab;
-    if (a.vocab % 256 == 0 && ((tiles_m + 1) / 2) * (cols / 256) >= 3 * (sms / 2))
-        return launch_pair<256, 6>(a, ma, tiles_m, sms, stream);
+    // (three stages of two 64-deep K slices each: 0.115 ms at 4096 rows against
+    // 0.122 with six stages of one slice, the same bytes in flight with half the
+    // stage hand-overs)
+    if (a.vocab % 256 == 0 && a.dim % (2 * kBK) == 0 &&
+        ((tiles_m + 1) / 2) * (cols / 256) >= 3 * (sms / 2))
+        return launch_pair<256, 3, 2>(a, ma, tiles_m, sms, stream);
     auto waves = [&](long long tiles, int slots) { return (tiles + slots - 1) / slots; };
     long long best = -1;
     int pick = 64;
@@ -928,9 +951,17 @@ cudaError_t launch_head_tc_bf16(const HeadArgs &a, cudaStream_t stream)
             pick = bn;
         }
     }
-    if (pick == 256) return launch_bn<256, 4>(a, ma, tiles_m, sms, stream);
-    if (pick == 128) return launch_bn<128, 6>(a, ma, tiles_m, sms, stream);
-    return launch_bn<64, 8>(a, ma, tiles_m, sms, stream);
+    // Stages of two 64-deep K slices where three or more such stages fit (BN 128
+    // and 64: 0.013 against 0.017 ms at 256 rows, 0.012 against 0.016 at 128);
+    // with BN 256 they would leave two stages, and four of one slice measure
+    // faster (0.019 against 0.021 ms at 512 rows).
+    const bool two = a.dim % (2 * kBK) == 0;
+    if (pick == 256) return launch_bn<256, 4, 1>(a, ma, tiles_m, sms, stream);
+    if (pick == 128)
+        return two ? launch_bn<128, 3, 2>(a, ma, tiles_m, sms, stream)
+                   : launch_bn<128, 6, 1>(a, ma, tiles_m, sms, stream);
+    return two ? launch_bn<64, 4, 2>(a, ma, tiles_m, sms, stream)
+               : launch_bn<64, 8, 1>(a, ma, tiles_m, sms, stream);
 }
 
 }  // namespace z2
