@@ -71,10 +71,10 @@ def test_out_norm_cfg_f32(z2, oracle, cuda, S, cfg):
 
 @pytest.mark.parametrize("S,cfg", [(128, 2.0), (256, None), (512, 1.5), (1024, 1.25)])
 def test_out_norm_cfg_bf16(z2, oracle, cuda, S, cfg):
-    """bf16 tensor-core head: S=128 pairs (N tile 128), S=256 (N tile 256) and
-    512 pairs (1024 hidden rows, N tile 256) on the one-SM kernel; 1024 pairs
-    (2048 hidden rows) on the two-SM kernel, whose epilogue stores 16 blended
-    output rows per 32-row chunk."""
+    """bf16 tensor-core head: S=128 pairs and S=256 (256 hidden rows) on the
+    one-SM kernel with 128-wide N tiles; 512 and 1024 pairs (1024 and 2048
+    hidden rows) on the two-SM kernel, whose epilogue stores 16 blended output
+    rows per 32-row chunk."""
     import torch
     rs = np.random.default_rng(9 + S)
     D = 2048

@@ -70,11 +70,11 @@ def test_head_bf16_tcgen05(z2, oracle, cuda, B, rpc):
 @pytest.mark.parametrize("B,rpc", [(4096, 1024), (2000, 1026), (2100, 1024), (1000, 1026),
                                    (1100, 1024)])
 def test_head_bf16_large_batch_rows(z2, oracle, cuda, B, rpc):
-    """Large batches: 4096, 2000 and 2100 rows on the two-SM kernel (256 x 256
-    tiles over CTA pairs, both accumulators; 2000 and 2100 leave the last tile
-    ragged, 2100 with an odd count of 128-row blocks), 1000 and 1100 on the
-    one-SM kernel with 256-wide N tiles, ragged too: rows spot-checked against
-    the oracle, every row against a torch f32 matmul of the same bf16 values."""
+    """Large batches on the two-SM kernel (256 x 256 tiles over CTA pairs, both
+    accumulators, two K slices per stage): 2000, 2100, 1000 and 1100 rows leave
+    the last tile ragged, 2100 and 1100 with an odd count of 128-row blocks.  Rows
+    spot-checked against the oracle, every row against a torch f32 matmul of the
+    same bf16 values."""
     import torch
     rs = np.random.default_rng(11 + B)
     Wb, Wf = _bf16(rs.normal(0, 0.02, size=(9 * rpc, 2048)).astype(np.float32))

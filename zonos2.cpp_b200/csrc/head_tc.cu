@@ -917,27 +917,29 @@ cudaError_t launch_head_tc_bf16(const HeadArgs &a, cudaStream_t stream)
     if (!make_map(&ma, a.hidden, (uint64_t)a.batch, (uint64_t)a.dim, kBM))
         return cudaErrorInvalidValue;
     const int tiles_m = (a.batch + kBM - 1) / kBM;
-    // Tile choice.  Two-SM pairs once each pair gets three or more 256 x 256 tiles
-    // (tensor-bound: a pair moves 128 + 128 operand rows per SM per tile).
+    // Tile choice.  Two-SM pairs (stages of two 64-deep K slices: the same bytes in
+    // flight as six one-slice stages, half the hand-overs) once half the pairs get
+    // a 256 x 256 tile; a pair moves 128 + 128 operand rows per SM per tile.
     // Below that the one-SM kernel, its N tile by a model of operand traffic: a
     // tile rereads its A rows once per N tile and its B rows once per M tile, so a
     // wave costs about (128 + BN) rows per SM and the launch ceil(tiles / SMs)
-    // waves; ties go to the wider tile.  Measured on a B200 (ms, 9 x 1024 x 2048):
+    // waves; ties go to the wider tile.  Measured on a B200 (ms, 9 x 1024 x 2048;
+    // pairs with two slices per stage, the one-SM kernel with BN 256 with one,
+    // 128 and 64 with two):
     //   rows   pairs   BN 256  BN 128  BN 64
-    //    128     -     0.0185  0.0184  0.0177
-    //    256   0.0227  0.0204  0.0191  0.0282
-    //    512   0.0237  0.0206  0.0306  0.0495
-    //   1024   0.0386  0.0369  0.0531  0.0915
-    //   2048   0.0669  0.0683    -       -
-    //   4096   0.1268  0.1305    -       -
-    // Pairs with 128-wide tiles (128 + 64 rows per SM) measured slower still:
-    // 0.0217 ms at 256 rows, 0.0354 at 512, 0.0592 at 1024.
+    //    128     -     0.0185  0.0184  0.0121
+    //    256     -     0.0204  0.0133  0.0282
+    //    384   0.0186  0.0189    -       -
+    //    512   0.0185  0.0188    -       -
+    //    768   0.0308  0.0337    -       -
+    //   1024   0.0321  0.0354    -       -
+    //   1536   0.0466  0.0515    -       -
+    //   4096   0.115   0.1305    -       -
+    // Pairs with 128-wide tiles (128 + 64 rows per SM) measured slower: 0.0217 ms at
+    // 256 rows, 0.0354 at 512, 0.0592 at 1024 (one slice per stage).
     const int cols = a.n_cb * a.vocab;
-    // (three stages of two 64-deep K slices each: 0.115 ms at 4096 rows against
-    // 0.122 with six stages of one slice, the same bytes in flight with half the
-    // stage hand-overs)
     if (a.vocab % 256 == 0 && a.dim % (2 * kBK) == 0 &&
-        ((tiles_m + 1) / 2) * (cols / 256) >= 3 * (sms / 2))
+        ((tiles_m + 1) / 2) * (cols / 256) >= sms / 4)
         return launch_pair<256, 3, 2>(a, ma, tiles_m, sms, stream);
     auto waves = [&](long long tiles, int slots) { return (tiles + slots - 1) / slots; };
     long long best = -1;
