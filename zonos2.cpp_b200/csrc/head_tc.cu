@@ -936,7 +936,8 @@ cudaError_t launch_head_tc_bf16(const HeadArgs &a, cudaStream_t stream)
     //   1536   0.0466  0.0515    -       -
     //   4096   0.115   0.1305    -       -
     // Pairs with 128-wide tiles (128 + 64 rows per SM) measured slower: 0.0217 ms at
-    // 256 rows, 0.0354 at 512, 0.0592 at 1024 (one slice per stage).
+    // 256 rows, 0.0354 at 512, 0.0592 at 1024 (one slice per stage); 0.0151 at 256
+    // and 0.0147 at 130 with two slices per stage, three stages or four.
     const int cols = a.n_cb * a.vocab;
     if (a.vocab % 256 == 0 && a.dim % (2 * kBK) == 0 &&
         ((tiles_m + 1) / 2) * (cols / 256) >= sms / 4)
