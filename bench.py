@@ -9,8 +9,9 @@ top-k 100, top-p 0.9, min-p 0.02, T 0.7, repetition penalty 1.1 over a
 1024-entry history per row.  A step samples one batch of logits for every
 stream; the delay step cycles through a 128-step rollout.  Streams are
 batch-sharded: each of N ranks owns 4096 streams (weak scaling) and the int32
-codes are all-gathered over NCCL every 8 steps (every step in e2e).  Logits and history (151 MB
-each per rank) exceed the 126 MB L2, so no flush is needed between steps.
+codes are all-gathered over NCCL every 32 steps (every step in e2e).  Logits and
+history (151 MB each per rank) exceed the 126 MB L2, so no flush is needed
+between steps.
 
 The line printed by rank 0 carries: ``value`` (device-resident inputs,
 CUDA-event timed, max over ranks), ``e2e`` (host logits -> codes on the host
@@ -46,7 +47,7 @@ METRIC = "sampled codes/sec (streams×9 codebooks) at B=4096; % HBM roofline; 1/
 STREAMS, NCB, VOCAB, HIST = 4096, 9, 1024, 1024
 TOPK, TOPP, MINP, TEMP, RHO, PAD = 100, 0.9, 0.02, 0.7, 1.1, 1023
 ROLLOUT = 128
-GATHER_EVERY = 8   # device-resident loop: steps of codes per all-gather
+GATHER_EVERY = 32  # device-resident loop: steps of codes per all-gather
 WORKLOAD = ("constrained sampling, 4096 streams x 9 codebooks x 1024 vocab per GPU: f32 "
             "logits ~N(0,4^2), 1% +8 spikes, softcap 15; delay masks over a 128-step rollout; "
             "70% allow bitmask; top-k 100, top-p 0.9, min-p 0.02, T 0.7; penalty 1.1 over "
