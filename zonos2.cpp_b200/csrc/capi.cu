@@ -107,10 +107,19 @@ int launch_rows(const float *logits, int n_streams, int n_cb, int vocab, long lo
     return ZONOS2CU_OK;
 }
 
+// n elements of device memory; *p is written only on success
+template <class T>
+cudaError_t dev_alloc(T **p, size_t n)
+{
+    void *q = nullptr;
+    const cudaError_t e = cudaMalloc(&q, sizeof(T) * n);
+    if (e == cudaSuccess) *p = static_cast<T *>(q);
+    return e;
+}
+
 // ---- per-device staging for the sample_token drop-in --------------------
-struct Staging {
+struct Staging {   // each member is created on first use and kept until exit
     std::mutex mu;
-    bool ready = false;
     cudaStream_t stream = nullptr;
     float *logits = nullptr;    // [1024]
     uint64_t *rng = nullptr;    // [4]
@@ -191,14 +200,16 @@ int zonos2cu_sample_token(uint64_t rng_state[4], const float *logits, int vocab_
     if (dev < 0 || dev >= 64) return ZONOS2CU_EINVAL;
     Staging &st = g_staging[dev];
     std::lock_guard<std::mutex> lock(st.mu);
-    if (!st.ready) {
-        // first call on this device: a small staging area, kept until exit
-        Z2_CK(cudaStreamCreateWithFlags(&st.stream, cudaStreamNonBlocking));
-        Z2_CK(cudaMalloc(&st.logits, sizeof(float) * z2::kSamplerVocabMax));
-        Z2_CK(cudaMalloc(&st.rng, sizeof(uint64_t) * 4));
-        Z2_CK(cudaMalloc(&st.out, sizeof(int32_t) * 2));
-        st.ready = true;
+    // first call on this device: a small staging area (a call that failed part way
+    // keeps what it made, and the next one makes the rest)
+    if (!st.stream) {
+        cudaStream_t s = nullptr;
+        Z2_CK(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+        st.stream = s;
     }
+    if (!st.logits) Z2_CK(dev_alloc(&st.logits, z2::kSamplerVocabMax));
+    if (!st.rng) Z2_CK(dev_alloc(&st.rng, 4));
+    if (!st.out) Z2_CK(dev_alloc(&st.out, 2));
     Z2_CK(cudaMemcpyAsync(st.logits, logits, sizeof(float) * vocab_size, cudaMemcpyHostToDevice,
                           st.stream));
     Z2_CK(cudaMemcpyAsync(st.rng, rng_state, sizeof(uint64_t) * 4, cudaMemcpyHostToDevice,

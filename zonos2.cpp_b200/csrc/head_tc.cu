@@ -810,27 +810,32 @@ template <int BN, int STAGES, int KSUB>
 cudaError_t launch_pair(const HeadArgs &a, const CUtensorMap &ma, int tiles_m, int sms,
                         cudaStream_t stream)
 {
-    static bool attr[64] = {false};
-    static int pairs_cap[64] = {0};   // clusters of two that fit at once
+    static std::mutex mu;
+    static int pairs_cap[64] = {0};   // clusters of two that fit at once; 0 until queried
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     // stages, 4 KB of output staging per epilogue warp, barriers, alignment
     const size_t smem =
         (size_t)STAGES * KSUB * (kBM + BN / 2) * kBK * 2 + (kEpiThreads / 32) * 4096 + 1024 + 512;
-    if (dev < 64 && !attr[dev]) {
-        e = cudaFuncSetAttribute(head_tc2_kernel<BN, STAGES, KSUB>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(2 * (sms / 2));
-        cfg.blockDim = dim3(kThreads);
-        cfg.dynamicSmemBytes = smem;
-        int n = 0;
-        e = cudaOccupancyMaxActiveClusters(&n, head_tc2_kernel<BN, STAGES, KSUB>, &cfg);
-        if (e != cudaSuccess) return e;
-        pairs_cap[dev] = n > 0 ? n : 1;
-        attr[dev] = true;
+    int pairs = 0;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (pairs_cap[dev] == 0) {
+            e = cudaFuncSetAttribute(head_tc2_kernel<BN, STAGES, KSUB>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(2 * (sms / 2));
+            cfg.blockDim = dim3(kThreads);
+            cfg.dynamicSmemBytes = smem;
+            int n = 0;
+            e = cudaOccupancyMaxActiveClusters(&n, head_tc2_kernel<BN, STAGES, KSUB>, &cfg);
+            if (e != cudaSuccess) return e;
+            pairs_cap[dev] = n > 0 ? n : 1;
+        }
+        pairs = pairs_cap[dev];
     }
     CUtensorMap mb;   // each CTA of a pair loads half of the tile's BN weight rows
     if (!make_map(&mb, a.W, (uint64_t)a.n_cb * a.rows_per_cb, (uint64_t)a.dim, BN / 2))
@@ -853,7 +858,6 @@ cudaError_t launch_pair(const HeadArgs &a, const CUtensorMap &ma, int tiles_m, i
     if (!make_map_f32(&mo, a.out, (uint64_t)t.out_rows, (uint64_t)a.n_cb * a.vocab,
                       a.cfg ? 16 : 32))
         return cudaErrorInvalidValue;
-    const int pairs = dev < 64 ? pairs_cap[dev] : 1;
     const int grid = 2 * (t.n_tiles < pairs ? t.n_tiles : pairs);
     return launch_pdl(head_tc2_kernel<BN, STAGES, KSUB>, grid, smem, stream, ma, mb, mo, t);
 }
@@ -862,18 +866,23 @@ template <int BN, int STAGES, int KSUB>
 cudaError_t launch_bn(const HeadArgs &a, const CUtensorMap &ma, int tiles_m, int sms,
                       cudaStream_t stream)
 {
-    static bool attr[64] = {false};
+    static std::mutex mu;
+    static bool attr[64] = {false};   // the shared-memory size has been set on the device
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     // stages, 4 KB of output staging per epilogue warp, barriers, alignment
     const size_t smem =
         (size_t)STAGES * KSUB * (kBM + BN) * kBK * 2 + (kEpiThreads / 32) * 4096 + 1024 + 512;
-    if (dev < 64 && !attr[dev]) {
-        e = cudaFuncSetAttribute(head_tc_kernel<BN, STAGES, KSUB>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        attr[dev] = true;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (!attr[dev]) {
+            e = cudaFuncSetAttribute(head_tc_kernel<BN, STAGES, KSUB>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+            attr[dev] = true;
+        }
     }
     CUtensorMap mb;
     if (!make_map(&mb, a.W, (uint64_t)a.n_cb * a.rows_per_cb, (uint64_t)a.dim, BN))
