@@ -2,7 +2,8 @@
 
 The reference arm runs on the host cores (the reference's own `sample_token`,
 compiled from its sources), so it is checked on the CPU; the CUDA arm is checked
-on a short run on the GPU, and through the lines kept under `profiles/`.
+through the lines kept under `profiles/` here, and on a short run on the GPU in
+`test_zzz_full_size_gpu.py`.
 """
 import json
 import math
@@ -99,14 +100,3 @@ def test_reference_arm_line():
         pytest.skip(d["unavailable"])
     check_reference(d)
     assert d["steps"] == 1 and d["n_gpus"] == 1
-
-
-@pytest.mark.gpu
-def test_cuda_arm_line():
-    p = subprocess.run([sys.executable, "bench.py", "--steps", "5", "--warmup", "3",
-                        "--no-cpu-baseline", "--no-head"], cwd=REPO, capture_output=True,
-                       text=True, timeout=900)
-    assert p.returncode == 0, p.stderr[-2000:]
-    d = last_json_line(p.stdout)
-    check_ours(d)
-    assert d["n_gpus"] == 1 and d["steps"] == 5 and d["cpu_baseline"] is None

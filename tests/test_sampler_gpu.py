@@ -277,42 +277,6 @@ def test_context_rollout_and_host_path(z2, oracle, cuda):
     ctx.close()
 
 
-def test_context_full_size_bench_workload(z2, oracle, cuda):
-    """The benchmark's per-GPU workload at full size -- 4096 streams x 9 x 1024,
-    config-4 knobs, a 1024-entry history and 70% allow bits -- through the
-    context as `bench.py` drives it (the first step primes the uniforms, the next
-    ones use those drawn ahead by the sampler's own CTAs).  Every code, flag,
-    generator state and history entry must equal the oracle's, step by step."""
-    import torch
-    import workloads as W
-    cfg = W.CONFIGS[4]
-    S, Cb = 4096, 9
-    ctx = z2.Context(0, S, Cb, 1024, 0, cfg.hist_len, seed=cfg.seed)
-    hist = W.initial_history(cfg, S)
-    ctx.set_history(hist, 0)
-    allow = W.allow_bits(cfg, S)
-    ctx.set_allow(allow)
-    prm = make_params(cfg.temperature, cfg.top_k, cfg.top_p, cfg.min_p, cfg.penalty, W.PAD)
-    p = z2.SampleParams(cfg.temperature, cfg.top_k, cfg.top_p, cfg.min_p, cfg.penalty, W.PAD)
-    rng = oracle.rng_seed_streams(cfg.seed, S)
-    codes = torch.full((S, Cb), -7, dtype=torch.int32, device=cuda)
-    flags = torch.full((S, Cb), -7, dtype=torch.int32, device=cuda)
-    for i, delay in enumerate((7, 8, 9)):   # codebook 8 forced to PAD at delay step 7
-        lg = W.step_logits(cfg, delay, S)
-        oc, of, _ = oracle.step(lg, prm, rng, hist, hist_pos=i, allow=allow, delay_step=delay,
-                                exp_mode=1)
-        ctx.sample(_t(lg, cuda), p, codes, flags, delay_step=delay)
-        torch.cuda.synchronize()
-        gc = codes.cpu().numpy()
-        bad = np.argwhere(gc != oc)
-        assert len(bad) == 0, f"step {i}: {len(bad)} token mismatches, first {bad[:5].tolist()}"
-        assert (flags.cpu().numpy() == of).all(), i
-        assert (ctx.get_rng() == rng).all(), i
-    h, pos = ctx.get_history()
-    assert pos == 3 and (h == hist).all()
-    ctx.close()
-
-
 @pytest.mark.parametrize("H", [1, 6, 37, 1024])
 def test_context_incremental_history_rollout(z2, oracle, cuda, H):
     """The context keeps token counts + a presence bitmap instead of scanning the

@@ -5,7 +5,8 @@ fixed array inside the library; here it must give exactly what the two entry
 points it stands for give -- zonos2cu_head_softcap into a caller buffer, then
 zonos2cu_sample_rows -- on two calls in a row (the array is reused).
 
-Collected last on purpose; it needs nothing from the other tests.
+Collected after the small-case parity tests on purpose; it needs nothing from
+the other tests.
 """
 import ctypes as C
 
