@@ -192,7 +192,9 @@ int zonos2cu_set_cfg(zonos2cu_ctx *ctx, int enable, float scale);
  * history position advances by one (mod hist_len) on success.  The host-path
  * calls below run on the context's own stream (zonos2cu_ctx_stream): work a
  * caller enqueues on other streams is not ordered with them, so synchronise
- * between the two kinds of call. */
+ * between the two kinds of call.  Each step reads what the step before it wrote
+ * (generator states, history, the uniforms drawn ahead): a context's steps go on
+ * one stream, or on streams the caller orders with events. */
 int zonos2cu_ctx_sample(zonos2cu_ctx *ctx, const float *logits_dev, long long row_stride,
                         const zonos2cu_sample_params *params, int delay_step,
                         int32_t *codes_dev, int32_t *flags_dev, void *stream);
