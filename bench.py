@@ -9,17 +9,21 @@ top-k 100, top-p 0.9, min-p 0.02, T 0.7, repetition penalty 1.1 over a
 1024-entry history per row.  A step samples one batch of logits for every
 stream; the delay step cycles through a 128-step rollout.  Streams are
 batch-sharded: each of N ranks owns 4096 streams (weak scaling) and the int32
-codes are all-gathered over NCCL every 32 steps (every step in e2e).  Logits and
-history (151 MB each per rank) exceed the 126 MB L2, so no flush is needed
-between steps.
+codes are collected on rank 0 through the library's NCCL gather
+(zonos2cu_gather_codes) every 32 steps and after the last (every step in e2e).
+Logits and history (151 MB each per rank) exceed the 126 MB L2, so no flush is
+needed between steps.
 
 The line printed by rank 0 carries: ``value`` (device-resident inputs,
-CUDA-event timed, max over ranks), ``e2e`` (host logits -> codes on the host
-through the library's public host API, copies inside the timed region),
-``roofline`` of the sampler kernel against the measured HBM copy bandwidth,
-``cpu_baseline`` (the reference's own sample_token, compiled unmodified,
-timed on this host), ``clocks`` sampled through NVML during the timed
-regions, and ``gpu_launches``.
+CUDA-event timed over the whole timed region, max over ranks), ``e2e`` (host
+logits -> codes on the host through the library's public host API, copies
+inside the timed region), ``roofline`` of the sampler kernel against the
+measured HBM copy bandwidth, ``cpu_baseline`` (the reference's own
+sample_token, compiled unmodified, timed on this host), ``fused`` (the
+batch-sharded fused configuration: bf16 head GEMM + softcap + sampler over 4096
+streams per rank, at every N), ``multi_gpu_check`` (N > 1: rank 0's gathered
+codes against a one-GPU context over the whole global batch), ``clocks``
+sampled through NVML during the timed regions, and ``gpu_launches``.
 
 ``--impl reference`` times the reference's CPU implementation of the same
 workload (oracle/_ref: the unmodified reference sources plus the build-defined
@@ -28,6 +32,7 @@ penalty / mask prologue) on all host cores; rank 0 only.
 from __future__ import annotations
 
 import argparse
+import hashlib
 import json
 import os
 import statistics
@@ -44,30 +49,38 @@ for p in (REPO, PKG):
         sys.path.insert(0, p)
 
 METRIC = "sampled codes/sec (streams×9 codebooks) at B=4096; % HBM roofline; 1/2/4/8 GPU"
-STREAMS, NCB, VOCAB, HIST = 4096, 9, 1024, 1024
+STREAMS, NCB, VOCAB, HIST, DIM = 4096, 9, 1024, 1024, 2048
 TOPK, TOPP, MINP, TEMP, RHO, PAD = 100, 0.9, 0.02, 0.7, 1.1, 1023
 ROLLOUT = 128
-GATHER_EVERY = 32  # device-resident loop: steps of codes per all-gather
+GATHER_EVERY = 32  # device-resident loops: steps of codes per gather to rank 0
+VERIFY_STEPS = 3   # N > 1: steps compared against a one-GPU run of the global batch
 WORKLOAD = ("constrained sampling, 4096 streams x 9 codebooks x 1024 vocab per GPU: f32 "
             "logits ~N(0,4^2), 1% +8 spikes, softcap 15; delay masks over a 128-step rollout; "
             "70% allow bitmask; top-k 100, top-p 0.9, min-p 0.02, T 0.7; penalty 1.1 over "
             "1024-entry history")
+FUSED_WORKLOAD = ("batch-sharded fused step, 4096 streams per GPU (32768 at 8 GPUs): hidden "
+                  "bf16 [4096, 2048] ~N(0,1) redrawn each step, heads bf16 [9*1024, 2048] "
+                  "~N(0,0.02^2), f32 accumulate, softcap 15; penalty 1.2 over 1024-entry "
+                  "history, top-k 50, top-p 0.95, min-p 0.02, T 0.7, seed 2024")
 # Algorithmic bytes of one (stream, codebook) row, the scope table's figure:
 # logits read + history read + token write and history append + allow bits
 # (one 128-byte mask per stream, shared by its 9 rows).
 ROW_BYTES = 4 * VOCAB + 4 * HIST + 8 + 128 / NCB
+FUSED_ROW_BYTES = 4 * VOCAB + 4 * HIST + 8        # no allow bits in the fused configuration
 # What the decode context actually has to move per row: logits, the 128-byte
 # presence bitmap of the history instead of the ring, ring read + write,
 # two u16 counts read and written, code and flag, allow bits, generator state.
 DESIGN_ROW_BYTES = 4 * VOCAB + 128 + 8 + 8 + 8 + 128 / NCB + 64 / NCB
 # DRAM bytes (read + write) of one sample_rows_kernel launch on this workload,
 # from an ncu capture of `bench.py --steps 12 --warmup 3 --no-cpu-baseline
-# --no-head`, launch 11 (dram__bytes_read.sum 167.17 MB +
-# dram__bytes_write.sum 7.11 MB).
+# --no-head --no-fused`, launch 11 (dram__bytes_read.sum + dram__bytes_write.sum).
 SAMPLER_TRAFFIC_BYTES = 174.28e6
 # Kernels of ours per decode step: the persistent sampler (the decode context
 # draws each step's uniforms during the step before).
 LAUNCHES_PER_STEP = 1
+# Spin ahead of each timed region, so the host has queued the region's launches
+# before its start event fires (the first launch does not wait on the host).
+LEAD_CYCLES = 4_000_000
 
 
 def dist_env():
@@ -75,6 +88,13 @@ def dist_env():
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     return ws, rank, local
+
+
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
 
 
 # ---------------------------------------------------------------------------
@@ -130,10 +150,13 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 def cpu_reference_run(steps: int, warmup: int, streams: int, seed: int = 1234):
     """The reference's own sample_token (oracle/_ref) over `streams` streams of
-    the workload per step, all host threads; returns (codes/s, threads, secs/step)."""
+    the workload per step, on every host core (the thread count is passed
+    explicitly: under torchrun OMP_NUM_THREADS is 1); returns (codes/s,
+    threads, secs/step)."""
     import workloads as W
-    from oracle import Reference, make_params
+    from oracle import Oracle, Reference, make_params
     R = Reference()
+    threads = host_cores()
     cfg = W.CONFIGS[4]
     prm = make_params(TEMP, TOPK, TOPP, MINP, RHO, PAD)
     rs = np.random.default_rng(seed)
@@ -142,20 +165,20 @@ def cpu_reference_run(steps: int, warmup: int, streams: int, seed: int = 1234):
         x = rs.normal(0.0, 4.0, size=(streams, NCB, VOCAB))
         x[rs.random(x.shape) < 0.01] = 8.0
         batches.append((15.0 * np.tanh(x / 15.0)).astype(np.float32))
+        del x
     hist = W.initial_history(cfg, streams)
     allow = W.allow_bits(cfg, streams)
-    from oracle import Oracle
     rng = Oracle().rng_seed_streams(seed, streams)
     for t in range(warmup):
         R.step(batches[t % 2], prm, rng, hist, hist_pos=t % HIST, allow=allow,
-               delay_step=t % ROLLOUT)
+               delay_step=t % ROLLOUT, nthreads=threads)
     t0 = time.perf_counter()
     for i in range(steps):
         t = warmup + i
         R.step(batches[t % 2], prm, rng, hist, hist_pos=t % HIST, allow=allow,
-               delay_step=t % ROLLOUT)
+               delay_step=t % ROLLOUT, nthreads=threads)
     dt = time.perf_counter() - t0
-    return streams * NCB * steps / dt, R.num_threads(), dt / max(steps, 1)
+    return streams * NCB * steps / dt, threads, dt / max(steps, 1)
 
 
 def run_reference(args):
@@ -185,7 +208,8 @@ def run_reference(args):
 
 # ---------------------------------------------------------------------------
 def make_device_inputs(torch, dev, rank: int, n_batches: int = 2):
-    """Config-4 inputs for this rank's 4096 streams, generated on the device."""
+    """Config-4 inputs of rank `rank`'s 4096 streams, the logits generated on
+    `dev` (a rank's inputs are the same whichever device makes them)."""
     import workloads as W
     g = torch.Generator(device=dev)
     g.manual_seed(1234 + 7919 * rank)
@@ -202,67 +226,64 @@ def make_device_inputs(torch, dev, rank: int, n_batches: int = 2):
     return batches, hist, allow
 
 
-def _bf16_peak():
+def _peaks():
     try:
         with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
-            return float(json.load(f).get("bf16_tflops", 1590.0))
+            return json.load(f), "measured"
     except Exception:
-        return 1590.0
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
 
 
 def time_head_gemm(torch, Z, dev, stream, Wt, B, g, reps: int = 20, warm: int = 3):
     """CUDA-event time of the bf16 head GEMM + softcap at batch B (ms/launch)."""
-    h = torch.randn((B, 2048), generator=g, device=dev).to(torch.bfloat16)
+    h = torch.randn((B, DIM), generator=g, device=dev).to(torch.bfloat16)
     lg = torch.empty((B, NCB, VOCAB), dtype=torch.float32, device=dev)
     for _ in range(warm):
         Z.head_softcap(Wt, Z.BF16, VOCAB, NCB, VOCAB, h, lg, stream=stream)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda._sleep(LEAD_CYCLES)
     e0.record(stream)
     for _ in range(reps):
         Z.head_softcap(Wt, Z.BF16, VOCAB, NCB, VOCAB, h, lg, stream=stream)
     e1.record(stream)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / max(reps, 1)
-    tflops = 2.0 * B * 2048 * NCB * VOCAB / (ms / 1e3) / 1e12
-    return {"ms": ms, "tflops": tflops, "frac_of_bf16_peak": tflops / _bf16_peak()}
+    tflops = 2.0 * B * DIM * NCB * VOCAB / (ms / 1e3) / 1e12
+    peak = float(_peaks()[0].get("bf16_tflops", 1590.0))
+    return {"ms": ms, "tflops": tflops, "frac_of_bf16_peak": tflops / peak}
 
 
 def head_weights_dev(torch, dev, g):
-    return (torch.randn((NCB * VOCAB, 2048), generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    return (torch.randn((NCB * VOCAB, DIM), generator=g, device=dev) * 0.02).to(torch.bfloat16)
 
 
 def measure_head(torch, Z, dev, stream, reps: int = 20):
     """The tcgen05 head GEMM (bf16, f32 accumulate, softcap epilogue) at the
-    fused configurations' batch sizes, and the fused decode step at 4096
-    streams (head + sampler, penalty 1.2 over 1024, top-k 50, top-p 0.95)."""
-    import workloads as W
+    fused configurations' batch sizes."""
     out = {}
     g = torch.Generator(device=dev)
     g.manual_seed(2024)
     Wt = head_weights_dev(torch, dev, g)
     for B in (256, 4096):
         out[f"gemm_b{B}"] = time_head_gemm(torch, Z, dev, stream, Wt, B, g, reps)
-    # the fused decode step, 4096 streams
-    S = 4096
-    cfg = W.CONFIGS[5]
-    ctx = Z.Context(dev.index, S, NCB, VOCAB, 2048, HIST, seed=cfg.seed)
-    ctx.set_head(W.to_bf16_bits(W.head_weights(cfg, rows_per_cb=VOCAB)), Z.BF16, VOCAB)
-    ctx.set_history(W.initial_history(cfg, S), 0)
-    p = Z.SampleParams(cfg.temperature, cfg.top_k, cfg.top_p, cfg.min_p, cfg.penalty, PAD)
-    h = torch.randn((S, 2048), generator=g, device=dev).to(torch.bfloat16)
-    codes = torch.zeros((S, NCB), dtype=torch.int32, device=dev)
-    for _ in range(3):
-        ctx.step(h, Z.BF16, p, codes, stream=stream)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(reps):
-        ctx.step(h, Z.BF16, p, codes, stream=stream)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / reps
-    out["fused_step_b4096"] = {"ms": ms, "codes_per_s": S * NCB / (ms / 1e3)}
-    ctx.close()
     return out
+
+
+def measure_drop_in(Z, frames: int = 20):
+    """Host-side latency of the sample_token drop-in (one row per call, 9 calls
+    per frame as the reference's loop makes them)."""
+    rs = np.random.default_rng(3)
+    rows = (15 * np.tanh(rs.normal(0, 3, (frames + 2, NCB, 1026)) / 15)).astype(np.float32)
+    rng = Z.Xoshiro256(42)
+    for cb in range(NCB):
+        Z.sample_token(rng, rows[0, cb], 1024, 0.7, 50, 0.9, 0.02)
+    t0 = time.perf_counter()
+    for f in range(frames):
+        for cb in range(NCB):
+            Z.sample_token(rng, rows[2 + f, cb], 1024, 0.7, 50, 0.9, 0.02)
+    dt = time.perf_counter() - t0
+    return {"us_per_call": dt / (frames * NCB) * 1e6, "us_per_frame": dt / frames * 1e6,
+            "frames": frames}
 
 
 def run_head_only(args):
@@ -283,164 +304,363 @@ def run_head_only(args):
         sys.exit(1)
 
 
-def run_ours(args):
-    import torch
-    import torch.distributed as dist
-    import sharding
-    import zonos2cu as Z
+# ---------------------------------------------------------------------------
+class Job:
+    """One rank's view of the batch-sharded job: torch.distributed for the
+    host-side plumbing (barriers, the timing max), the library's own NCCL
+    communicator for the codes gather to rank 0."""
 
-    ws, rank, local = dist_env()
-    first, _ = sharding.shard_range(ws * STREAMS, ws, rank)
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if ws > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)
+    def __init__(self, torch, Z):
+        import torch.distributed as dist
+        self.torch, self.Z, self.dist = torch, Z, dist
+        self.ws, self.rank, self.local = dist_env()
+        torch.cuda.set_device(self.local)
+        self.dev = torch.device("cuda", self.local)
+        self.stream = torch.cuda.current_stream()
+        self.comm = None
+        if self.ws > 1:
+            import datetime
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=self.dev)
+            box = [Z.comm_unique_id() if self.rank == 0 else None]
+            dist.broadcast_object_list(box, src=0)
+            self.comm = Z.Comm(self.local, self.ws, self.rank, box[0])
 
-    def barrier():
-        if ws > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
+    def barrier(self):
+        if self.ws > 1:
+            self.dist.barrier()
+        self.torch.cuda.synchronize()
 
-    batches, hist, allow = make_device_inputs(torch, dev, rank)
-    ctx = Z.Context(local, STREAMS, NCB, VOCAB, 0, HIST, seed=1234, first_stream=first)
+    def aligned_start(self, ev):
+        """Records `ev` on every rank once all have reached it on the device:
+        a spin, then a one-element all-reduce, ahead of the start event."""
+        self.torch.cuda._sleep(LEAD_CYCLES)
+        if self.ws > 1:
+            t = self.torch.ones(1, device=self.dev)
+            self.dist.all_reduce(t)
+        ev.record(self.stream)
+
+    def max_over_ranks(self, *vals):
+        if self.ws == 1:
+            return vals
+        t = self.torch.tensor(vals, device=self.dev, dtype=self.torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return tuple(float(x) for x in t.tolist())
+
+    def gather(self, ring, n_steps, out):
+        """n_steps of this rank's codes [n_steps][STREAMS][NCB] to rank 0."""
+        if self.ws > 1 and n_steps > 0:
+            self.comm.gather_codes(0, ring, n_steps, self.ws * STREAMS, NCB,
+                                   out if self.rank == 0 else None, stream=self.stream)
+
+    def close(self):
+        if self.comm is not None:
+            self.torch.cuda.synchronize()
+            self.comm.close()
+        if self.ws > 1:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
+
+
+def codes_digest(a: np.ndarray) -> str:
+    return hashlib.sha256(np.ascontiguousarray(a, np.int32).tobytes()).hexdigest()[:16]
+
+
+def multi_gpu_check(job, params):
+    """Rank 0's gathered codes of VERIFY_STEPS steps of the sharded run against
+    one context over the whole global batch on rank 0's GPU (same inputs, same
+    generators): every code must match."""
+    torch, Z, ws, rank = job.torch, job.Z, job.ws, job.rank
+    import workloads as W
+    first, count = Z.shard_range(ws * STREAMS, ws, rank)
+    batches, hist, allow = make_device_inputs(torch, job.dev, rank)
+    ctx = Z.Context(job.local, count, NCB, VOCAB, 0, HIST, seed=1234, first_stream=first)
     ctx.set_history(hist, 0)
     ctx.set_allow(allow)
-    params = Z.SampleParams(TEMP, TOPK, TOPP, MINP, RHO, PAD)
-    codes = torch.zeros((STREAMS, NCB), dtype=torch.int32, device=dev)
-    flags = torch.zeros((STREAMS, NCB), dtype=torch.int32, device=dev)
-    gathered = torch.zeros((ws * STREAMS, NCB), dtype=torch.int32, device=dev)
-    stream = torch.cuda.current_stream()
+    ring = torch.zeros((VERIFY_STEPS, count, NCB), dtype=torch.int32, device=job.dev)
+    for t in range(VERIFY_STEPS):
+        ctx.sample(batches[t % 2], params, ring[t], delay_step=t, stream=job.stream)
+    out = None
+    if rank == 0:
+        out = torch.zeros((ws * VERIFY_STEPS * STREAMS * NCB,), dtype=torch.int32, device=job.dev)
+    job.gather(ring, VERIFY_STEPS, out)
+    job.torch.cuda.synchronize()
+    ctx.close()
+    del batches
+    result = None
+    if rank == 0:
+        got = out.view(ws, VERIFY_STEPS, STREAMS, NCB).permute(1, 0, 2, 3).reshape(
+            VERIFY_STEPS, ws * STREAMS, NCB).cpu().numpy()
+        N = ws * STREAMS
+        whole = Z.Context(job.local, N, NCB, VOCAB, 0, HIST, seed=1234, first_stream=0)
+        parts = [make_device_inputs(torch, job.dev, r) for r in range(ws)]
+        whole.set_history(np.concatenate([p[1] for p in parts]), 0)
+        whole.set_allow(np.concatenate([p[2] for p in parts]))
+        glog = [torch.cat([p[0][b] for p in parts]) for b in range(2)]
+        del parts
+        codes = torch.zeros((N, NCB), dtype=torch.int32, device=job.dev)
+        want = np.zeros((VERIFY_STEPS, N, NCB), np.int32)
+        for t in range(VERIFY_STEPS):
+            whole.sample(glog[t % 2], params, codes, delay_step=t, stream=job.stream)
+            torch.cuda.synchronize()
+            want[t] = codes.cpu().numpy()
+        whole.close()
+        del glog
+        mism = int((got != want).sum())
+        result = {"steps": VERIFY_STEPS, "global_streams": N, "rows": int(want.size),
+                  "mismatches": mism, "sha256_16_gathered": codes_digest(got),
+                  "sha256_16_one_gpu": codes_digest(want),
+                  "what": "rank 0's gathered codes of the sharded run vs one context over the "
+                          "whole global batch on rank 0's GPU"}
+        torch.cuda.empty_cache()
+    job.barrier()
+    return result
 
-    def gather():
-        sharding.gather_codes(codes, ws * STREAMS, ws, rank, out=gathered)
 
-    # The device-resident loop keeps each step's codes in a ring of GATHER_EVERY
-    # steps and all-gathers the ring to every rank once it is full (and at the
-    # end): rank 0 collects output, which needs no per-step round trip.
-    ring = torch.zeros((GATHER_EVERY, STREAMS, NCB), dtype=torch.int32, device=dev)
-    ring_all = torch.zeros((ws, GATHER_EVERY, STREAMS, NCB), dtype=torch.int32, device=dev)
+def time_sampler(job, params, steps, warmup, clocks):
+    """The config-4 sampler loop: (total_ms, per-launch event ms, launches)."""
+    torch = job.torch
+    batches, hist, allow = make_device_inputs(torch, job.dev, job.rank)
+    first, count = job.Z.shard_range(job.ws * STREAMS, job.ws, job.rank)
+    ctx = job.Z.Context(job.local, count, NCB, VOCAB, 0, HIST, seed=1234, first_stream=first)
+    ctx.set_history(hist, 0)
+    ctx.set_allow(allow)
+    flags = torch.zeros((STREAMS, NCB), dtype=torch.int32, device=job.dev)
+    ring = torch.zeros((GATHER_EVERY, STREAMS, NCB), dtype=torch.int32, device=job.dev)
+    out = None
+    if job.rank == 0 and job.ws > 1:
+        out = torch.zeros((job.ws * GATHER_EVERY * STREAMS * NCB,), dtype=torch.int32,
+                          device=job.dev)
 
-    def ring_step(t, i, n):
-        ctx.sample(batches[t % len(batches)], params, ring[i % GATHER_EVERY], flags,
-                   delay_step=t % ROLLOUT, stream=stream)
+    def run(t0, n):
+        filled = 0
+        for i in range(n):
+            t = t0 + i
+            ctx.sample(batches[t % 2], params, ring[i % GATHER_EVERY], flags,
+                       delay_step=t % ROLLOUT, stream=job.stream)
+            filled += 1
+            if filled == GATHER_EVERY or i == n - 1:
+                job.gather(ring, filled, out)
+                filled = 0
 
-    def ring_flush(i, n):
-        if ws > 1 and ((i + 1) % GATHER_EVERY == 0 or i == n - 1):
-            dist.all_gather_into_tensor(ring_all, ring)
-
-    clocks = ClockSampler(local) if rank == 0 else None
-
-    # ---- device-resident timing -------------------------------------------
-    for t in range(args.warmup):
-        ring_step(t, t, args.warmup)
-        ring_flush(t, args.warmup)
-    barrier()
+    run(0, warmup)
+    job.barrier()
     if clocks:
         clocks.active.set()
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
-    t_start.record(stream)
-    for i in range(args.steps):
-        ring_step(args.warmup + i, i, args.steps)
-        ring_flush(i, args.steps)
-    t_end.record(stream)
-    barrier()
-    # The sampler's own launch time (the roofline's denominator), from events
-    # around each step's two launches, in a second pass of the same steps so the
-    # events do not sit inside the throughput measurement.
-    n_ev = args.steps
-    k_start = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
-    k_end = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
-    for i in range(n_ev):
-        k_start[i].record(stream)
-        ring_step(args.warmup + args.steps + i, i, n_ev)
-        k_end[i].record(stream)
-        ring_flush(i, n_ev)
-    barrier()
+    job.aligned_start(t_start)
+    run(warmup, steps)
+    t_end.record(job.stream)
+    job.barrier()
+    # Events around each launch, in a second pass (they break the programmatic
+    # overlap of back-to-back launches, so they stay out of the timed region).
+    ks = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ke = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for i in range(steps):
+        ks[i].record(job.stream)
+        ctx.sample(batches[i % 2], params, ring[i % GATHER_EVERY], flags,
+                   delay_step=(warmup + steps + i) % ROLLOUT, stream=job.stream)
+        ke[i].record(job.stream)
+    job.barrier()
     if clocks:
         clocks.active.clear()
     total_ms = t_start.elapsed_time(t_end)
-    kern_ms = sum(a.elapsed_time(b) for a, b in zip(k_start, k_end)) / max(n_ev, 1)
-    if ws > 1:
-        tt = torch.tensor([total_ms, kern_ms], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        total_ms, kern_ms = float(tt[0]), float(tt[1])
-    rows = STREAMS * NCB
-    value = rows * ws * args.steps / (total_ms / 1e3)
+    ev_ms = sum(a.elapsed_time(b) for a, b in zip(ks, ke)) / max(steps, 1)
+    ctx.close()
+    return (batches, hist, allow), total_ms, ev_ms
 
-    # ---- end to end: host logits -> host codes ------------------------------
+
+def time_e2e(job, params, inputs, steps, clocks):
+    """Host logits -> host codes: pinned host logits copied in, the sampler,
+    codes collected on rank 0 and copied out, every step."""
+    torch = job.torch
+    batches, hist, allow = inputs
+    first, count = job.Z.shard_range(job.ws * STREAMS, job.ws, job.rank)
+    ctx = job.Z.Context(job.local, count, NCB, VOCAB, 0, HIST, seed=1234, first_stream=first)
+    ctx.set_history(hist, 0)
+    ctx.set_allow(allow)
     host_batches = [b.cpu().pin_memory() for b in batches]
-    host_codes = torch.zeros((ws, STREAMS, NCB), dtype=torch.int32).pin_memory()
+    host_codes = torch.zeros((job.ws * STREAMS, NCB), dtype=torch.int32).pin_memory()
     host_flags = torch.zeros((STREAMS, NCB), dtype=torch.int32).pin_memory()
     dev_in = torch.empty_like(batches[0])
+    codes = torch.zeros((STREAMS, NCB), dtype=torch.int32, device=job.dev)
+    flags = torch.zeros((STREAMS, NCB), dtype=torch.int32, device=job.dev)
+    gathered = torch.zeros((job.ws * STREAMS, NCB), dtype=torch.int32, device=job.dev)
 
-    def e2e_step(t):
-        hb = host_batches[t % len(host_batches)]
-        if ws == 1:
-            ctx.sample_host(hb.numpy(), params, host_codes[0].numpy(), host_flags.numpy(),
+    def step(t):
+        hb = host_batches[t % 2]
+        if job.ws == 1:
+            ctx.sample_host(hb.numpy(), params, host_codes.numpy(), host_flags.numpy(),
                             delay_step=t % ROLLOUT)
         else:
             dev_in.copy_(hb, non_blocking=True)
-            ctx.sample(dev_in, params, codes, flags, delay_step=t % ROLLOUT, stream=stream)
-            gather()
-            if rank == 0:
-                host_codes.view(ws * STREAMS, NCB).copy_(gathered, non_blocking=True)
-            stream.synchronize()
+            ctx.sample(dev_in, params, codes, flags, delay_step=t % ROLLOUT, stream=job.stream)
+            job.gather(codes, 1, gathered)
+            if job.rank == 0:
+                host_codes.copy_(gathered, non_blocking=True)
+            job.stream.synchronize()
 
-    e2e_steps = max(1, min(args.steps, 64))
     for t in range(2):
-        e2e_step(t)
-    barrier()
+        step(t)
+    job.barrier()
     if clocks:
         clocks.active.set()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
+    e0.record(job.stream)
     w0 = time.perf_counter()
-    for i in range(e2e_steps):
-        e2e_step(args.warmup + i)
-    e1.record(stream)
+    for i in range(steps):
+        step(2 + i)
+    e1.record(job.stream)
     torch.cuda.synchronize()
     wall_ms = (time.perf_counter() - w0) * 1e3
     if clocks:
         clocks.active.clear()
-    e2e_ms = max(e0.elapsed_time(e1), wall_ms)
-    if ws > 1:
-        tt = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        e2e_ms = float(tt[0])
-    e2e_value = rows * ws * e2e_steps / (e2e_ms / 1e3)
-    h2d = int(batches[0].numel() * 4)
-    d2h = int(rows * 4 * (2 if ws == 1 else ws)) if rank == 0 else 0
-
+    ms = max(e0.elapsed_time(e1), wall_ms)
     ctx.close()
-    head = measure_head(torch, Z, dev, stream) if (rank == 0 and not args.no_head) else None
+    return ms
+
+
+def time_fused(job, steps, warmup, clocks):
+    """The batch-sharded fused configuration: per rank 4096 streams, bf16
+    head GEMM + softcap + sampler per step (zonos2cu_ctx_step), codes to rank 0
+    every 32 steps.  Returns the timed region's ms and the head / sampler
+    kernel times from a second pass with events between the two kernels."""
+    torch, Z = job.torch, job.Z
+    import workloads as W
+    cfg = W.CONFIGS[5]
+    first, count = Z.shard_range(job.ws * STREAMS, job.ws, job.rank)
+    ctx = Z.Context(job.local, count, NCB, VOCAB, DIM, HIST, seed=cfg.seed, first_stream=first)
+    ctx.set_head(W.to_bf16_bits(W.head_weights(cfg, rows_per_cb=VOCAB)), Z.BF16, VOCAB)
+    ctx.set_history(W.initial_history(cfg, count, first=first), 0)
+    p = Z.SampleParams(cfg.temperature, cfg.top_k, cfg.top_p, cfg.min_p, cfg.penalty, PAD)
+    g = torch.Generator(device=job.dev)
+    g.manual_seed(cfg.seed + 7919 * job.rank)
+    hidden = [torch.randn((count, DIM), generator=g, device=job.dev).to(torch.bfloat16)
+              for _ in range(2)]
+    ring = torch.zeros((GATHER_EVERY, count, NCB), dtype=torch.int32, device=job.dev)
+    out = None
+    if job.rank == 0 and job.ws > 1:
+        out = torch.zeros((job.ws * GATHER_EVERY * STREAMS * NCB,), dtype=torch.int32,
+                          device=job.dev)
+
+    def run(t0, n):
+        filled = 0
+        for i in range(n):
+            ctx.step(hidden[(t0 + i) % 2], Z.BF16, p, ring[i % GATHER_EVERY], stream=job.stream)
+            filled += 1
+            if filled == GATHER_EVERY or i == n - 1:
+                job.gather(ring, filled, out)
+                filled = 0
+
+    run(0, warmup)
+    job.barrier()
+    if clocks:
+        clocks.active.set()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    job.aligned_start(t0)
+    run(warmup, steps)
+    t1.record(job.stream)
+    job.barrier()
+    if clocks:
+        clocks.active.clear()
+    total_ms = t0.elapsed_time(t1)
+    # the two kernels apart, with events around each: the head GEMM on the same
+    # bf16 weights into a logits buffer, then the context's sampler on it
+    Wt = torch.from_numpy(W.to_bf16_bits(W.head_weights(cfg, rows_per_cb=VOCAB)).view(
+        np.int16)).to(job.dev).view(torch.bfloat16)
+    lg = torch.empty((count, NCB, VOCAB), dtype=torch.float32, device=job.dev)
+    n_ev = min(steps, 10)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(n_ev)]
+    for i in range(n_ev):
+        ev[i][0].record(job.stream)
+        Z.head_softcap(Wt, Z.BF16, VOCAB, NCB, VOCAB, hidden[i % 2], lg, stream=job.stream)
+        ev[i][1].record(job.stream)
+        ctx.sample(lg, p, ring[i % GATHER_EVERY], stream=job.stream)
+        ev[i][2].record(job.stream)
+    job.barrier()
+    head_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / n_ev
+    sampler_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / n_ev
+    ctx.close()
+    return total_ms, head_ms, sampler_ms
+
+
+def run_ours(args):
+    import torch
+    import zonos2cu as Z
+
+    job = Job(torch, Z)
+    ws, rank = job.ws, job.rank
+    params = Z.SampleParams(TEMP, TOPK, TOPP, MINP, RHO, PAD)
+    clocks = ClockSampler(job.local) if rank == 0 else None
+
+    check = multi_gpu_check(job, params) if ws > 1 and not args.no_check else None
+
+    inputs, total_ms, ev_ms = time_sampler(job, params, args.steps, args.warmup, clocks)
+    total_ms, ev_ms = job.max_over_ranks(total_ms, ev_ms)
+    rows = STREAMS * NCB
+    value = rows * ws * args.steps / (total_ms / 1e3)
+
+    e2e_steps = max(1, min(args.steps, 64))
+    e2e_ms = job.max_over_ranks(time_e2e(job, params, inputs, e2e_steps, clocks))[0]
+    e2e_value = rows * ws * e2e_steps / (e2e_ms / 1e3)
+    h2d = int(inputs[0][0].numel() * 4)
+    d2h = int(rows * 4 * (2 if ws == 1 else ws)) if rank == 0 else 0
+    del inputs
+    torch.cuda.empty_cache()
+
+    fused = None
+    if not args.no_fused:
+        f_total, head_ms, f_samp = time_fused(job, args.steps, args.warmup, clocks)
+        f_total, head_ms, f_samp = job.max_over_ranks(f_total, head_ms, f_samp)
+        peaks, src = _peaks()
+        flops = 2.0 * STREAMS * DIM * NCB * VOCAB
+        fused = {
+            "workload": FUSED_WORKLOAD, "streams_per_gpu": STREAMS, "n_gpus": ws,
+            "steps": args.steps, "ms_per_step": f_total / args.steps,
+            "codes_per_s": rows * ws * args.steps / (f_total / 1e3),
+            "gather": f"codes to rank 0 every {GATHER_EVERY} steps and after the last",
+            "sampler_ms_events": f_samp,
+            "head_ms_events": head_ms,
+            "head_tflops": flops / (head_ms / 1e3) / 1e12,
+            "head_frac_of_bf16_peak": flops / (head_ms / 1e3) / 1e12 /
+                                      float(peaks.get("bf16_tflops", 1590.0)),
+            "sampler_gbs": FUSED_ROW_BYTES * rows / (f_samp / 1e3) / 1e9,
+            "sampler_frac_of_hbm": FUSED_ROW_BYTES * rows / (f_samp / 1e3) / 1e9 /
+                                   float(peaks.get("hbm_gbs", 6650.0)),
+            "peak_source": src,
+            "kernels": "head_ms / sampler_ms from events around each kernel in a second pass "
+                       "(the head on the same weights into a logits buffer, then the sampler)",
+        }
+
+    head = drop_in = None
+    if rank == 0 and ws == 1 and not args.no_head:
+        head = measure_head(torch, Z, job.dev, job.stream)
+        drop_in = measure_drop_in(Z)
+
     if rank != 0:
-        if ws > 1:
-            dist.barrier()
-            dist.destroy_process_group()
+        job.close()
         return
 
-    peaks = {}
-    try:
-        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
-            peaks = json.load(f)
-    except Exception:
-        pass
+    peaks, peak_src = _peaks()
     peak = float(peaks.get("hbm_gbs", 6650.0))
-    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
     launch_bytes = ROW_BYTES * rows
+    # The sampler's mean launch time: over the whole timed region at one GPU (it
+    # holds nothing but the sampler's launches), from the per-launch events where
+    # the region also holds the gathers.
+    kern_ms = total_ms / args.steps if ws == 1 else ev_ms
     achieved = launch_bytes / (kern_ms / 1e3) / 1e9
 
     cpu = None
     if ws == 1 and not args.no_cpu_baseline:
         try:
-            cv, threads, _ = cpu_reference_run(steps=3, warmup=1, streams=args.cpu_streams)
+            cv, threads, _ = cpu_reference_run(steps=args.cpu_steps, warmup=2, streams=STREAMS)
             cpu = {"value": cv, "unit": "codes/s", "cores": threads, "kind": "reference",
-                   "sample": f"{args.cpu_streams} streams x {NCB} rows x 3 steps of the same "
-                             f"workload (unmodified reference sample_token, OpenMP)"}
+                   "sample": f"{args.cpu_steps} full steps of {STREAMS} streams x {NCB} rows of "
+                             f"the same workload (unmodified reference sample_token, OpenMP "
+                             f"on {threads} threads)"}
         except Exception as e:
             cpu = {"value": None, "unit": "codes/s", "cores": 0, "kind": "reference",
                    "sample": f"unavailable: {type(e).__name__}: {e}"}
@@ -452,13 +672,17 @@ def run_ours(args):
         "data": "synthetic",
         "config": {"workload": WORKLOAD, "streams_per_gpu": STREAMS, "codebooks": NCB,
                    "vocab": VOCAB,
-                   "parallelism": f"batch-sharded x{ws}, NCCL all-gather of the codes every "
-                                  f"{GATHER_EVERY} steps (per step in e2e)",
+                   "parallelism": f"batch-sharded x{ws}, codes gathered to rank 0 over NCCL "
+                                  f"(zonos2cu_gather_codes) every {GATHER_EVERY} steps and "
+                                  f"after the last (every step in e2e)",
                    "l2": "inputs larger than L2 (151 MB logits + 151 MB history per GPU per step)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": args.traffic,
                      "kernel": "sample_rows_kernel",
                      "kernel_ms": kern_ms,
+                     "kernel_ms_source": "timed region / launches" if ws == 1
+                                         else "events around each launch",
+                     "kernel_ms_events": ev_ms,
                      "bytes_per_launch": launch_bytes, "peak_source": peak_src,
                      "design_bytes_per_launch": DESIGN_ROW_BYTES * rows,
                      "design_frac": DESIGN_ROW_BYTES * rows / (kern_ms / 1e3) / 1e9 / peak},
@@ -466,13 +690,14 @@ def run_ours(args):
         "e2e": {"value": e2e_value, "unit": "codes/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps},
         "gpu_launches": LAUNCHES_PER_STEP * args.steps,
+        "fused": fused,
+        "multi_gpu_check": check,
         "head": head,
+        "drop_in": drop_in,
         "clocks": clocks.result() if clocks else None,
     }
     print(json.dumps(line), flush=True)
-    if ws > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    job.close()
 
 
 def main():
@@ -481,9 +706,11 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--cpu-streams", type=int, default=1024)
+    ap.add_argument("--cpu-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-head", action="store_true", help="skip the head GEMM / fused timing")
+    ap.add_argument("--no-head", action="store_true", help="skip the head GEMM timings")
+    ap.add_argument("--no-fused", action="store_true", help="skip the fused configuration")
+    ap.add_argument("--no-check", action="store_true", help="skip the N > 1 codes check")
     ap.add_argument("--head-only", type=int, default=0, metavar="B",
                     help="time only the bf16 head GEMM at batch B (profiling case)")
     ap.add_argument("--traffic", type=float, default=SAMPLER_TRAFFIC_BYTES,

@@ -13,9 +13,23 @@
  *     `stream` (NULL = the legacy default stream).  "_host" pointers are host
  *     memory; those calls copy in and out and return when the result is on the
  *     host.
- *   - The library allocates device memory only inside zonos2cu_ctx_create /
- *     zonos2cu_set_head (owned by the context) and on the first call of
- *     zonos2cu_sample_token on a device (a small per-device staging area).
+ *   - Device memory is allocated only by these calls:
+ *       zonos2cu_ctx_create, zonos2cu_set_head, zonos2cu_set_allow,
+ *       zonos2cu_set_out_norm, zonos2cu_set_embeddings, zonos2cu_gen_begin
+ *         (owned by the context, freed by zonos2cu_ctx_destroy);
+ *       the first zonos2cu_ctx_sample_host / zonos2cu_ctx_step_host of a
+ *         context, and a later one with larger inputs (host-path staging,
+ *         owned by the context);
+ *       the first zonos2cu_sample_token on a device (a small per-device
+ *         staging area, kept until exit);
+ *       zonos2cu_comm_create (NCCL's own buffers, freed by
+ *         zonos2cu_comm_destroy).
+ *     Every other entry point, zonos2cu_step_noalloc included, allocates
+ *     nothing.
+ *   - Host buffers given to the "_host" calls are copied with
+ *     cudaMemcpyAsync: page-locked memory (cudaHostAlloc, or
+ *     cudaHostRegister on an existing buffer) copies at full PCIe speed,
+ *     pageable memory (a plain std::vector) through a bounce buffer.
  *   - A context belongs to one device and is not thread-safe; use one per
  *     (device, host thread).
  *
@@ -46,6 +60,7 @@ extern "C" {
 #define ZONOS2CU_EUNSUPPORTED (-5) /* shape outside what the kernels implement     */
 #define ZONOS2CU_EDEVICE (-6)      /* a kernel reported a bounded wait that expired */
 #define ZONOS2CU_ETOOBIG (-7)      /* larger than zonos2cu_step_noalloc's fixed scratch */
+#define ZONOS2CU_ENCCL (-8)        /* NCCL is missing or an NCCL call failed        */
 
 /* ---- per-row flags written next to each sampled code ---------------------- */
 #define ZONOS2CU_FLAG_ALL_MASKED 1 /* no logit >= -1e9 survived: code = pad_id     */
@@ -265,6 +280,38 @@ int zonos2cu_write_codes_bin(const char *path, const int32_t *frames_host, int n
  * they expire (synchronises the current device).  0 = no error. */
 int zonos2cu_device_error(void);
 
+/* ---- several GPUs: batch-sharded streams, codes collected on one rank --------
+ * One process per GPU.  Rank r of n owns the contiguous slice [first, first +
+ * count) of the global batch that zonos2cu_shard_range gives (the first
+ * n_streams % n_ranks ranks own one stream more) and creates its context with
+ * that count and first_stream = first: its generators and codes then equal the
+ * same streams of a one-GPU run of the whole batch.  Nothing crosses GPUs but
+ * the codes, which the writer rank collects -- the frame collection of
+ * src/zonos2_generate.cpp:278, for a batch.  NCCL is loaded at run time
+ * (libnccl.so.2, or the copy the process already holds); without it these
+ * calls return ZONOS2CU_ENCCL and the rest of the library is unaffected. */
+int zonos2cu_shard_range(long long n_streams, int n_ranks, int rank, long long *first,
+                         long long *count);
+/* An NCCL communicator over the job's ranks (a ncclComm_t, as void *): rank 0
+ * makes the id, the caller hands it to every rank out of band (MPI, a file, a
+ * socket), then every rank calls zonos2cu_comm_create with it -- collectively,
+ * as ncclCommInitRank is.  A caller that has its own NCCL communicator passes
+ * that to zonos2cu_gather_codes instead. */
+int zonos2cu_comm_unique_id(unsigned char id[128]);
+int zonos2cu_comm_create(int device, int n_ranks, int rank, const unsigned char id[128],
+                         void **nccl_comm_out);
+int zonos2cu_comm_destroy(void *nccl_comm);
+/* Collects n_steps steps of codes on rank `root`, called by every rank of the
+ * communicator with the same root, n_steps, n_streams (the global batch) and
+ * n_cb, on `stream` (asynchronous; nothing is synchronised).  codes_dev is this
+ * rank's block [n_steps][count][n_cb] (e.g. a ring of per-step codes); out_dev
+ * (root only; others may pass NULL) receives every rank's block in rank
+ * order: rank r's at element n_steps * first_r * n_cb.  For n_steps = 1 that
+ * is the global [n_streams][n_cb].  Only the root receives: the other ranks
+ * send and return. */
+int zonos2cu_gather_codes(void *nccl_comm, int root, const int32_t *codes_dev, int n_steps,
+                          long long n_streams, int n_cb, int32_t *out_dev, void *stream);
+
 /* ---- one decode step that allocates nothing -------------------------------- */
 
 /* No counterpart in the reference.  For callers that may not allocate device
@@ -277,11 +324,16 @@ int zonos2cu_device_error(void);
  * until the process exits, and no call allocates or frees anything.
  *   - n_streams * n_cb * vocab must not exceed ZONOS2CU_NOALLOC_MAX_LOGITS
  *     (64 streams of 9 x 1024): larger requests return ZONOS2CU_ETOOBIG.
- *   - The first call on a device looks the array's device address up
- *     (cudaGetSymbolAddress, with that device current); make that first call
- *     before any stream capture.
+ *   - The array's device address belongs to the CUDA context current at the
+ *     call.  Outside stream capture each call looks it up (cudaGetSymbolAddress,
+ *     which allocates nothing); a call made while `stream` is capturing uses
+ *     the address found by the last call outside capture in the same context,
+ *     and returns ZONOS2CU_ESTATE if that context has made none.  So make one
+ *     call in a context before capturing it, and again after cudaDeviceReset.
  *   - All calls on a device share the one array: calls whose work overlaps on
  *     the GPU race.  Order them on one stream, or synchronise between them.
+ *   - Every argument is checked before anything is launched, as the two entry
+ *     points would check it (n_streams = 0 included).
  * Arguments are those of the two entry points it combines (softcap 15 in
  * the model; row stride of the logits = vocab). */
 #define ZONOS2CU_NOALLOC_MAX_LOGITS (64 * 9 * 1024)

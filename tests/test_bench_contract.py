@@ -3,7 +3,7 @@
 The reference arm runs on the host cores (the reference's own `sample_token`,
 compiled from its sources), so it is checked on the CPU; the CUDA arm is checked
 through the lines kept under `profiles/` here, and on a short run on the GPU in
-`test_zzz_full_size_gpu.py`.
+`test_z_full_size_gpu.py`.
 """
 import json
 import math

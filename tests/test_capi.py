@@ -119,3 +119,30 @@ def test_context_rejects_bad_dims(z2):
               z2.Dims(4, 9, 1024, 0, -3, 0, 0)):
         assert L.zonos2cu_ctx_create(0, C.byref(d), C.byref(h)) == z2.EINVAL
     assert L.zonos2cu_ctx_destroy(None) == 0
+
+
+def test_shard_range_matches_the_python_shard_arithmetic(z2):
+    import sharding
+    for n in (0, 1, 7, 4096, 32768, 32769, 100003):
+        for ws in (1, 2, 3, 4, 7, 8):
+            for r in range(ws):
+                assert z2.shard_range(n, ws, r) == sharding.shard_range(n, ws, r), (n, ws, r)
+    L = z2.lib()
+    f, c = C.c_longlong(), C.c_longlong()
+    assert L.zonos2cu_shard_range(10, 0, 0, C.byref(f), C.byref(c)) == z2.EINVAL
+    assert L.zonos2cu_shard_range(10, 2, 2, C.byref(f), C.byref(c)) == z2.EINVAL
+    assert L.zonos2cu_shard_range(-1, 2, 0, C.byref(f), C.byref(c)) == z2.EINVAL
+
+
+def test_gather_and_comm_reject_bad_arguments(z2):
+    """Checked before NCCL is touched (no GPU or NCCL needed)."""
+    L = z2.lib()
+    assert L.zonos2cu_gather_codes(None, 0, 1 << 20, 1, 8, 9, 1 << 21, None) == z2.EINVAL
+    assert L.zonos2cu_gather_codes(1 << 12, 0, 1 << 20, -1, 8, 9, 1 << 21, None) == z2.EINVAL
+    assert L.zonos2cu_gather_codes(1 << 12, 0, 1 << 20, 1, 8, 0, 1 << 21, None) == z2.EINVAL
+    h = C.c_void_p()
+    uid = bytes(128)
+    assert L.zonos2cu_comm_create(0, 0, 0, uid, C.byref(h)) == z2.EINVAL
+    assert L.zonos2cu_comm_create(0, 2, 2, uid, C.byref(h)) == z2.EINVAL
+    assert L.zonos2cu_comm_create(0, 1, 0, None, C.byref(h)) == z2.EINVAL
+    assert L.zonos2cu_comm_destroy(None) == 0

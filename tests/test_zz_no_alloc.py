@@ -28,6 +28,34 @@ def test_noalloc_rejects_requests_beyond_its_array(z2):
     assert rc == z2.ETOOBIG
 
 
+def test_noalloc_checks_sampler_arguments_before_any_launch(z2):
+    """Invalid sampler arguments are rejected as zonos2cu_sample_rows rejects
+    them -- with no stream at all, and before the head would be launched (the
+    pointers here are never dereferenced, so no GPU is needed)."""
+    L = z2.lib()
+    bad_t = z2.SampleParams(temperature=0.0)
+    bad_minp = z2.SampleParams(min_p=1.5)
+    good = z2.SampleParams()
+    W, h, rng, codes = 1 << 20, 1 << 21, 1 << 22, 1 << 23
+    for S in (0, 3):
+        for p in (bad_t, bad_minp):
+            rc = L.zonos2cu_step_noalloc(W, z2.BF16, 1024, 9, 1024, 2048, h, S, 15.0, C.byref(p),
+                                         rng, None, 0, 0, None, -1, codes, None, None)
+            assert rc == z2.EINVAL, (S, rc)
+            assert L.zonos2cu_sample_rows(256, S, 9, 1024, 1024, C.byref(p), rng, None, 0, 0,
+                                          None, -1, codes, None, None) == z2.EINVAL
+        # misaligned generator states, a history position outside the ring, too many codebooks
+        for args in ((rng + 8, None, 0, 0, 9), (rng, 1 << 24, 16, 16, 9), (rng, None, 0, 0, 17)):
+            r, hist, H, pos, ncb = args
+            rc = L.zonos2cu_step_noalloc(W, z2.BF16, 1024, ncb, 1024, 2048, h, S, 15.0,
+                                         C.byref(good), r, hist, H, pos, None, -1, codes, None,
+                                         None)
+            assert rc == z2.EINVAL, (S, args, rc)
+    # n_streams = 0 with valid arguments launches nothing and succeeds
+    assert L.zonos2cu_step_noalloc(W, z2.BF16, 1024, 9, 1024, 2048, h, 0, 15.0, C.byref(good),
+                                   rng, None, 0, 0, None, -1, codes, None, None) == 0
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("dtype,S,H", [("bf16", 64, 96), ("f32", 3, 0)])
 def test_noalloc_step_matches_head_then_sample(z2, oracle, cuda, dtype, S, H):

@@ -20,6 +20,19 @@ namespace {
 
 thread_local char tl_error[256] = "";
 
+}  // namespace
+
+// The message zonos2cu_last_error returns on this thread (the other .cu files
+// of the library report through it).
+__attribute__((visibility("hidden"))) const char *z2_set_error(const char *fmt, const char *a,
+                                                               const char *b)
+{
+    snprintf(tl_error, sizeof(tl_error), fmt, a, b);
+    return tl_error;
+}
+
+namespace {
+
 int cuda_fail(cudaError_t e, const char *what)
 {
     snprintf(tl_error, sizeof(tl_error), "%s: %s", what, cudaGetErrorString(e));
@@ -231,16 +244,26 @@ int zonos2cu_sample_token(uint64_t rng_state[4], const float *logits, int vocab_
 
 namespace {
 
+int check_head(const void *W_dev, zonos2cu_dtype dtype, int rows_per_cb, int n_cb, int vocab,
+               int dim, const void *hidden_dev, int batch, float softcap, const float *logits_dev)
+{
+    if (n_cb < 1 || vocab < 1 || dim < 1 || batch < 0 || rows_per_cb < vocab)
+        return ZONOS2CU_EINVAL;
+    if (isnan(softcap)) return ZONOS2CU_EINVAL;
+    if (dtype != ZONOS2CU_F32 && dtype != ZONOS2CU_BF16) return ZONOS2CU_EINVAL;
+    if (batch > 0 && (!W_dev || !hidden_dev || !logits_dev)) return ZONOS2CU_EINVAL;
+    return ZONOS2CU_OK;
+}
+
 // The head on `batch` hidden rows; with cfg, rows pair up and `logits_dev` gets
 // batch / 2 blended rows.
 int launch_head(const void *W_dev, zonos2cu_dtype dtype, int rows_per_cb, int n_cb, int vocab,
                 int dim, const void *hidden_dev, int batch, float softcap, float *logits_dev,
                 void *stream, bool cfg, float cfg_scale)
 {
-    if (n_cb < 1 || vocab < 1 || dim < 1 || batch < 0 || rows_per_cb < vocab)
-        return ZONOS2CU_EINVAL;
-    if (isnan(softcap)) return ZONOS2CU_EINVAL;
-    if (batch > 0 && (!W_dev || !hidden_dev || !logits_dev)) return ZONOS2CU_EINVAL;
+    int rc = check_head(W_dev, dtype, rows_per_cb, n_cb, vocab, dim, hidden_dev, batch, softcap,
+                        logits_dev);
+    if (rc) return rc;
     z2::HeadArgs a{W_dev, rows_per_cb, n_cb, vocab, dim, hidden_dev, batch, softcap, logits_dev};
     a.cfg = cfg ? 1 : 0;
     a.cfg_scale = cfg_scale;
@@ -258,6 +281,24 @@ int launch_head(const void *W_dev, zonos2cu_dtype dtype, int rows_per_cb, int n_
 }
 
 }  // namespace
+
+// Every check that zonos2cu_head_softcap and then zonos2cu_sample_rows would make
+// on these arguments, with `logits_dev` standing for the buffer between them:
+// zonos2cu_step_noalloc runs it before it launches anything.
+__attribute__((visibility("hidden"))) int z2_check_head_then_sample(
+    const void *W_dev, zonos2cu_dtype dtype, int rows_per_cb, int n_cb, int vocab, int dim,
+    const void *hidden_dev, int n_streams, float softcap, const float *logits_dev,
+    const zonos2cu_sample_params *params, uint64_t *rng_dev, int32_t *hist_dev, int hist_len,
+    int hist_pos, int32_t *codes_dev)
+{
+    int rc = check_head(W_dev, dtype, rows_per_cb, n_cb, vocab, dim, hidden_dev, n_streams,
+                        softcap, logits_dev);
+    if (rc) return rc;
+    rc = check_rows(logits_dev, n_streams, n_cb, vocab, vocab, rng_dev, hist_dev, hist_len,
+                    hist_pos, codes_dev);
+    if (rc) return rc;
+    return check_params(params, vocab);
+}
 
 extern "C" {
 

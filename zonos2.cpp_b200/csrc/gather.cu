@@ -1,0 +1,204 @@
+// gather.cu -- several GPUs: the batch-sharded decode job's codes collected on
+// one rank over NCCL.
+//
+// Decode streams are independent, so a job shards its global batch into
+// contiguous slices, one per rank (zonos2cu_shard_range), each rank's context
+// created with first_stream = its slice's start.  The only data that crosses
+// GPUs is the int32 codes, which the writer rank collects: the role of the
+// frame collection at src/zonos2_generate.cpp:278, for a batch.
+//
+// NCCL is loaded at run time (dlopen of libnccl.so.2, reusing a copy the
+// process already holds, e.g. PyTorch's), so the library loads and runs its
+// one-GPU entry points on hosts without NCCL.  The gather is grouped
+// point-to-point: every other rank sends its block to the root, the root
+// receives them all in one group and copies its own block on the stream.
+#include <dlfcn.h>
+#include <nccl.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "zonos2_cuda.h"
+
+const char *z2_set_error(const char *fmt, const char *a, const char *b);
+
+namespace {
+
+struct NcclApi {
+    bool tried = false;
+    bool ok = false;
+    ncclResult_t (*GetUniqueId)(ncclUniqueId *) = nullptr;
+    ncclResult_t (*CommInitRank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommCount)(const ncclComm_t, int *) = nullptr;
+    ncclResult_t (*CommUserRank)(const ncclComm_t, int *) = nullptr;
+    ncclResult_t (*Send)(const void *, size_t, ncclDataType_t, int, ncclComm_t,
+                         cudaStream_t) = nullptr;
+    ncclResult_t (*Recv)(void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*GroupStart)() = nullptr;
+    ncclResult_t (*GroupEnd)() = nullptr;
+    const char *(*GetErrorString)(ncclResult_t) = nullptr;
+};
+std::mutex g_nccl_mu;
+NcclApi g_nccl;
+
+template <class F>
+bool sym(void *h, const char *name, F *out)
+{
+    *out = reinterpret_cast<F>(dlsym(h, name));
+    return *out != nullptr;
+}
+
+// The NCCL entry points, loaded once; null if libnccl.so.2 cannot be found.
+const NcclApi *nccl()
+{
+    std::lock_guard<std::mutex> lk(g_nccl_mu);
+    if (g_nccl.tried) return g_nccl.ok ? &g_nccl : nullptr;
+    g_nccl.tried = true;
+    void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) {
+        z2_set_error("%s: %s", "dlopen libnccl.so.2", dlerror());
+        return nullptr;
+    }
+    NcclApi &a = g_nccl;
+    a.ok = sym(h, "ncclGetUniqueId", &a.GetUniqueId) && sym(h, "ncclCommInitRank", &a.CommInitRank) &&
+           sym(h, "ncclCommDestroy", &a.CommDestroy) && sym(h, "ncclCommCount", &a.CommCount) &&
+           sym(h, "ncclCommUserRank", &a.CommUserRank) && sym(h, "ncclSend", &a.Send) &&
+           sym(h, "ncclRecv", &a.Recv) && sym(h, "ncclGroupStart", &a.GroupStart) &&
+           sym(h, "ncclGroupEnd", &a.GroupEnd) && sym(h, "ncclGetErrorString", &a.GetErrorString);
+    if (!a.ok) z2_set_error("%s: %s", "libnccl.so.2", "an entry point is missing");
+    return a.ok ? &a : nullptr;
+}
+
+int nccl_fail(const NcclApi *a, ncclResult_t r, const char *what)
+{
+    z2_set_error("%s: %s", what, a->GetErrorString(r));
+    return ZONOS2CU_ENCCL;
+}
+
+#define Z2_NCCL(api, call)                                          \
+    do {                                                            \
+        const ncclResult_t r_ = (call);                             \
+        if (r_ != ncclSuccess) return nccl_fail(api, r_, #call);    \
+    } while (0)
+
+struct DeviceScope {
+    int prev = -1;
+    explicit DeviceScope(int dev)
+    {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceScope()
+    {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+}  // namespace
+
+extern "C" {
+
+int zonos2cu_shard_range(long long n_streams, int n_ranks, int rank, long long *first,
+                         long long *count)
+{
+    if (n_streams < 0 || n_ranks < 1 || rank < 0 || rank >= n_ranks || !first || !count)
+        return ZONOS2CU_EINVAL;
+    const long long base = n_streams / n_ranks, extra = n_streams % n_ranks;
+    *count = base + (rank < extra ? 1 : 0);
+    *first = rank * base + (rank < extra ? rank : extra);
+    return ZONOS2CU_OK;
+}
+
+int zonos2cu_comm_unique_id(unsigned char id[128])
+{
+    if (!id) return ZONOS2CU_EINVAL;
+    const NcclApi *a = nccl();
+    if (!a) return ZONOS2CU_ENCCL;
+    ncclUniqueId u;
+    Z2_NCCL(a, a->GetUniqueId(&u));
+    static_assert(sizeof(u.internal) == 128, "NCCL unique id size");
+    memcpy(id, u.internal, 128);
+    return ZONOS2CU_OK;
+}
+
+int zonos2cu_comm_create(int device, int n_ranks, int rank, const unsigned char id[128],
+                         void **comm_out)
+{
+    if (!id || !comm_out || n_ranks < 1 || rank < 0 || rank >= n_ranks) return ZONOS2CU_EINVAL;
+    *comm_out = nullptr;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev)
+        return ZONOS2CU_EINVAL;
+    const NcclApi *a = nccl();
+    if (!a) return ZONOS2CU_ENCCL;
+    DeviceScope g(device);
+    ncclUniqueId u;
+    memcpy(u.internal, id, 128);
+    ncclComm_t c = nullptr;
+    Z2_NCCL(a, a->CommInitRank(&c, n_ranks, u, rank));
+    *comm_out = c;
+    return ZONOS2CU_OK;
+}
+
+int zonos2cu_comm_destroy(void *comm)
+{
+    if (!comm) return ZONOS2CU_OK;
+    const NcclApi *a = nccl();
+    if (!a) return ZONOS2CU_ENCCL;
+    Z2_NCCL(a, a->CommDestroy(static_cast<ncclComm_t>(comm)));
+    return ZONOS2CU_OK;
+}
+
+int zonos2cu_gather_codes(void *comm, int root, const int32_t *codes_dev, int n_steps,
+                          long long n_streams, int n_cb, int32_t *out_dev, void *stream)
+{
+    if (!comm || n_steps < 0 || n_streams < 0 || n_cb < 1) return ZONOS2CU_EINVAL;
+    const NcclApi *a = nccl();
+    if (!a) return ZONOS2CU_ENCCL;
+    const ncclComm_t c = static_cast<ncclComm_t>(comm);
+    int n_ranks = 0, rank = 0;
+    Z2_NCCL(a, a->CommCount(c, &n_ranks));
+    Z2_NCCL(a, a->CommUserRank(c, &rank));
+    if (root < 0 || root >= n_ranks) return ZONOS2CU_EINVAL;
+    long long first = 0, count = 0;
+    zonos2cu_shard_range(n_streams, n_ranks, rank, &first, &count);
+    const size_t my_elems = (size_t)n_steps * (size_t)count * (size_t)n_cb;
+    if (my_elems > 0 && !codes_dev) return ZONOS2CU_EINVAL;
+    if (rank == root && n_steps > 0 && n_streams > 0 && !out_dev) return ZONOS2CU_EINVAL;
+    if (n_steps == 0 || n_streams == 0) return ZONOS2CU_OK;
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (rank != root) {
+        if (my_elems) Z2_NCCL(a, a->Send(codes_dev, my_elems, ncclInt32, root, c, st));
+        return ZONOS2CU_OK;
+    }
+    // the root: every other rank's block in rank order, its own copied in place
+    Z2_NCCL(a, a->GroupStart());
+    for (int r = 0; r < n_ranks; r++) {
+        long long f = 0, n = 0;
+        zonos2cu_shard_range(n_streams, n_ranks, r, &f, &n);
+        const size_t elems = (size_t)n_steps * (size_t)n * (size_t)n_cb;
+        if (r == root || elems == 0) continue;
+        const ncclResult_t res =
+            a->Recv(out_dev + (size_t)n_steps * (size_t)f * (size_t)n_cb, elems, ncclInt32, r, c, st);
+        if (res != ncclSuccess) {
+            a->GroupEnd();
+            return nccl_fail(a, res, "ncclRecv");
+        }
+    }
+    Z2_NCCL(a, a->GroupEnd());
+    int32_t *mine = out_dev + (size_t)n_steps * (size_t)first * (size_t)n_cb;
+    if (my_elems && mine != codes_dev) {
+        const cudaError_t e = cudaMemcpyAsync(mine, codes_dev, sizeof(int32_t) * my_elems,
+                                              cudaMemcpyDeviceToDevice, st);
+        if (e != cudaSuccess) {
+            z2_set_error("%s: %s", "root block copy", cudaGetErrorString(e));
+            return ZONOS2CU_ECUDA;
+        }
+    }
+    return ZONOS2CU_OK;
+}
+
+}  // extern "C"

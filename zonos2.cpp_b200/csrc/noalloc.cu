@@ -5,37 +5,91 @@
 //
 // The head writes its logits into a fixed array compiled into the library
 // instead of a caller or context buffer; the sampler reads them from there.
-// The array's device address is looked up once per device, on the first
-// call, with that device current.  Every call shares the array, so calls
-// whose work overlaps on the GPU race; nothing in it has to start at zero
-// (the head overwrites every logit the sampler reads).
+// Every call shares the array, so calls whose work overlaps on the GPU race;
+// nothing in it has to start at zero (the head overwrites every logit the
+// sampler reads).
+//
+// The array's device address belongs to the CUDA context current at the call.
+// Outside stream capture every call looks it up again (cudaGetSymbolAddress
+// allocates nothing), so a context made after cudaDeviceReset, or a different
+// context made current on the same device, gets its own address.  Under
+// capture no lookup is made: the address recorded by the last call outside
+// capture in the same context is used, and a context that has never made one
+// gets ZONOS2CU_ESTATE.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "zonos2_cuda.h"
+
+int z2_check_head_then_sample(const void *W_dev, zonos2cu_dtype dtype, int rows_per_cb, int n_cb,
+                              int vocab, int dim, const void *hidden_dev, int n_streams,
+                              float softcap, const float *logits_dev,
+                              const zonos2cu_sample_params *params, uint64_t *rng_dev,
+                              int32_t *hist_dev, int hist_len, int hist_pos, int32_t *codes_dev);
 
 namespace {
 
 static __device__ __align__(256) float g_noalloc_logits[ZONOS2CU_NOALLOC_MAX_LOGITS];
 
+using CtxGetCurrentFn = CUresult (*)(CUcontext *);
+
 struct ScratchAddr {
     std::mutex mu;
-    float *dev[64] = {};
+    bool looked_up = false;
+    CtxGetCurrentFn ctx_get_current = nullptr;
+    struct Entry {
+        CUcontext ctx;
+        float *addr;
+    };
+    Entry seen[64] = {};   // the address last found in each context, most recent first
+    int n_seen = 0;
 };
 ScratchAddr g_addr;
 
-// The array's device address on the current device (set up on first use).
-int scratch_on_current_device(float **out)
+// The context current on this thread (null if the driver entry point is missing).
+CUcontext current_context()
 {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ZONOS2CU_ECUDA;
+    if (!g_addr.looked_up) {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_addr.ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(fn);
+        g_addr.looked_up = true;
+    }
+    CUcontext c = nullptr;
+    if (!g_addr.ctx_get_current || g_addr.ctx_get_current(&c) != CUDA_SUCCESS) return nullptr;
+    return c;
+}
+
+// The array's device address in the current context.
+int scratch_in_current_context(cudaStream_t stream, float **out)
+{
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) return ZONOS2CU_ECUDA;
     std::lock_guard<std::mutex> lock(g_addr.mu);
-    if (!g_addr.dev[dev]) {
+    const CUcontext ctx = current_context();
+    if (cap == cudaStreamCaptureStatusNone) {
         void *p = nullptr;
         if (cudaGetSymbolAddress(&p, g_noalloc_logits) != cudaSuccess || !p) return ZONOS2CU_ECUDA;
-        g_addr.dev[dev] = static_cast<float *>(p);
+        *out = static_cast<float *>(p);
+        if (!ctx) return ZONOS2CU_OK;
+        int i = 0;   // record it, most recent first
+        while (i < g_addr.n_seen && g_addr.seen[i].ctx != ctx) i++;
+        if (i == g_addr.n_seen && g_addr.n_seen < 64) g_addr.n_seen++;
+        if (i == 64) i = 63;   // forget the oldest context
+        for (; i > 0; i--) g_addr.seen[i] = g_addr.seen[i - 1];
+        g_addr.seen[0] = {ctx, *out};
+        return ZONOS2CU_OK;
     }
-    *out = g_addr.dev[dev];
-    return ZONOS2CU_OK;
+    for (int i = 0; ctx && i < g_addr.n_seen; i++)
+        if (g_addr.seen[i].ctx == ctx) {
+            *out = g_addr.seen[i].addr;
+            return ZONOS2CU_OK;
+        }
+    return ZONOS2CU_ESTATE;
 }
 
 }  // namespace
@@ -48,12 +102,19 @@ extern "C" int zonos2cu_step_noalloc(const void *W_dev, zonos2cu_dtype dtype, in
                                      const uint32_t *allow_dev, int delay_step, int32_t *codes_dev,
                                      int32_t *flags_dev, void *stream)
 {
-    if (n_streams < 0 || n_cb < 1 || vocab < 1) return ZONOS2CU_EINVAL;
+    // Every argument is checked before anything is launched: an invalid sampler
+    // argument must not cost a head launch, nor overwrite the shared array.  The
+    // array's address stands in for the logits buffer (it is never null).
+    const float *placeholder = reinterpret_cast<const float *>(256);
+    int rc = z2_check_head_then_sample(W_dev, dtype, rows_per_cb, n_cb, vocab, dim, hidden_dev,
+                                       n_streams, softcap, placeholder, params, rng_dev, hist_dev,
+                                       hist_len, hist_pos, codes_dev);
+    if (rc) return rc;
     if ((long long)n_streams * n_cb * vocab > (long long)ZONOS2CU_NOALLOC_MAX_LOGITS)
         return ZONOS2CU_ETOOBIG;
     if (n_streams == 0) return ZONOS2CU_OK;
     float *logits = nullptr;
-    int rc = scratch_on_current_device(&logits);
+    rc = scratch_in_current_context((cudaStream_t)stream, &logits);
     if (rc) return rc;
     rc = zonos2cu_head_softcap(W_dev, dtype, rows_per_cb, n_cb, vocab, dim, hidden_dev, n_streams,
                                softcap, logits, stream);

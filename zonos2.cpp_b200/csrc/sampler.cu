@@ -30,21 +30,22 @@
 // bucket B* holding the k-th largest logit.  Buckets <= B*+1 are the
 // candidates: a superset of the top-k that also holds every logit whose
 // probability could round equal to the k-th one's (equal probabilities need
-// logits far closer than a bucket).  In the common case (<= 256 candidates)
-// they are scattered in bucket order, get an exact probability, and are put in
-// (p desc, token asc) order by ranking each one inside its bucket; an
-// adjacency check falls back to a bitonic sort if a probability tie straddles
-// a bucket edge.  One running prefix sum of the sorted probabilities serves
-// every sum the reference recomputes from zero, and lane 0 walks the CDFs over
-// quotients p / sum that the warp divides out 32 at a time.  Other rows (top-k
-// off, > 256 candidates) take a slower general path; delay-forced rows return
-// the pad token once the row has been checked for non-finite logits.
+// logits far closer than a bucket).  In the common case (<= 128 candidates)
+// they are scattered in bucket order as 32-bit keys, four per lane, and sorted
+// in registers; the decisions are certified on fixed-point prefix sums of
+// hardware-exp2 probabilities against the reference's own error margins, and
+// the rows no margin settles take an exact form out of line (exact
+// probabilities, f64 prefix sums, and where those cannot decide either, the
+// reference's f32 running sums term by term).  Other rows (top-k off, > 128
+// candidates) take a slower general path; delay-forced rows return the pad
+// token once the row has been checked for non-finite logits.
 //
-// Exactness: every f32 operation that decides the token is the reference's
-// own operation in the reference's order -- (l - max) / T, exp rounded
-// correctly to f32, sums accumulated one term at a time in sorted order,
-// p / sum divisions, the CDF walk -- so for equal inputs the token equals the
-// reference's up to (a) equal-probability ties, taken in ascending token
+// Exactness: the token is the one the reference's own f32 operations give --
+// (l - max) / T, exp rounded correctly to f32, sums accumulated one term at a
+// time in sorted order, p / sum divisions, the CDF walk -- either because a
+// certified margin shows the decision cannot differ or because those
+// operations are carried out as written; so for equal inputs the token equals
+// the reference's up to (a) equal-probability ties, taken in ascending token
 // order, and (b) the reference's expf being misrounded by one ulp (glibc, on
 // about 1e-4 of its inputs).  (l - max) / T is computed as an f64 product
 // with RN(1/T) rounded to f32: the f64 error (< 2^-52 relative) cannot reach

@@ -25,7 +25,8 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libzonos2cu.so")
 
-OK, EINVAL, ECUDA, ENOMEM, ESTATE, EUNSUPPORTED, EDEVICE, ETOOBIG = 0, -1, -2, -3, -4, -5, -6, -7
+OK, EINVAL, ECUDA, ENOMEM, ESTATE, EUNSUPPORTED, EDEVICE, ETOOBIG, ENCCL = (
+    0, -1, -2, -3, -4, -5, -6, -7, -8)
 NOALLOC_MAX_LOGITS = 64 * 9 * 1024
 FLAG_ALL_MASKED, FLAG_NONFINITE = 1, 2
 F32, BF16 = 0, 1
@@ -40,14 +41,17 @@ EXPORTS = (
     "zonos2cu_step_noalloc", "zonos2cu_set_out_norm", "zonos2cu_set_cfg",
     "zonos2cu_gen_begin", "zonos2cu_gen_end", "zonos2cu_gen_read", "zonos2cu_gen_next_input",
     "zonos2cu_gen_shear_up", "zonos2cu_set_embeddings", "zonos2cu_gen_embed_next",
-    "zonos2cu_embed_frames", "zonos2cu_write_codes_bin",
+    "zonos2cu_embed_frames", "zonos2cu_write_codes_bin", "zonos2cu_shard_range",
+    "zonos2cu_comm_unique_id", "zonos2cu_comm_create", "zonos2cu_comm_destroy",
+    "zonos2cu_gather_codes",
 )
 
 
 class Zonos2cuError(RuntimeError):
     def __init__(self, code: int, what: str):
         names = {EINVAL: "EINVAL", ECUDA: "ECUDA", ENOMEM: "ENOMEM", ESTATE: "ESTATE",
-                 EUNSUPPORTED: "EUNSUPPORTED", EDEVICE: "EDEVICE", ETOOBIG: "ETOOBIG"}
+                 EUNSUPPORTED: "EUNSUPPORTED", EDEVICE: "EDEVICE", ETOOBIG: "ETOOBIG",
+                 ENCCL: "ENCCL"}
         msg = f"{what} failed: {names.get(code, code)}"
         detail = last_error() if _lib is not None else ""
         if detail:
@@ -120,6 +124,11 @@ def lib() -> C.CDLL:
         "zonos2cu_device_error": (i, []),
         "zonos2cu_step_noalloc": (i, [vp, i, i, i, i, i, vp, i, f, C.POINTER(SampleParams), vp,
                                       vp, i, i, vp, i, vp, vp, vp]),
+        "zonos2cu_shard_range": (i, [ll, i, i, C.POINTER(ll), C.POINTER(ll)]),
+        "zonos2cu_comm_unique_id": (i, [C.c_char_p]),
+        "zonos2cu_comm_create": (i, [i, i, i, C.c_char_p, C.POINTER(vp)]),
+        "zonos2cu_comm_destroy": (i, [vp]),
+        "zonos2cu_gather_codes": (i, [vp, i, vp, i, ll, i, vp, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -223,6 +232,45 @@ def step_noalloc(W, dtype: int, rows_per_cb: int, n_cb: int, vocab: int, hidden,
                                      _ptr(allow), delay_step, _ptr(codes), _ptr(flags),
                                      _stream(stream))
     _check(rc, "zonos2cu_step_noalloc")
+
+
+def shard_range(n_streams: int, n_ranks: int, rank: int) -> tuple[int, int]:
+    """(first global stream, number of streams) of `rank`'s slice."""
+    first, count = C.c_longlong(), C.c_longlong()
+    _check(lib().zonos2cu_shard_range(n_streams, n_ranks, rank, C.byref(first), C.byref(count)),
+           "zonos2cu_shard_range")
+    return first.value, count.value
+
+
+def comm_unique_id() -> bytes:
+    """A fresh NCCL unique id (128 bytes), made on the job's first rank."""
+    buf = C.create_string_buffer(128)
+    _check(lib().zonos2cu_comm_unique_id(buf), "zonos2cu_comm_unique_id")
+    return buf.raw
+
+
+class Comm:
+    """An NCCL communicator made by the library (zonos2cu_comm_create); every
+    rank creates it collectively with the id rank 0 made."""
+
+    def __init__(self, device: int, n_ranks: int, rank: int, uid: bytes):
+        if len(uid) != 128:
+            raise ValueError("an NCCL unique id is 128 bytes")
+        h = C.c_void_p()
+        _check(lib().zonos2cu_comm_create(device, n_ranks, rank, uid, C.byref(h)),
+               "zonos2cu_comm_create")
+        self.h, self.n_ranks, self.rank = h, n_ranks, rank
+
+    def gather_codes(self, root: int, codes, n_steps: int, n_streams: int, n_cb: int, out=None,
+                     stream=None) -> None:
+        """Rank `root` receives every rank's [n_steps][count][n_cb] block in rank order."""
+        _check(lib().zonos2cu_gather_codes(self.h, root, _ptr(codes), n_steps, n_streams, n_cb,
+                                           _ptr(out), _stream(stream)), "zonos2cu_gather_codes")
+
+    def close(self) -> None:
+        if self.h:
+            _check(lib().zonos2cu_comm_destroy(self.h), "zonos2cu_comm_destroy")
+            self.h = C.c_void_p()
 
 
 def device_error() -> int:
