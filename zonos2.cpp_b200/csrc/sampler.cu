@@ -720,6 +720,26 @@ __device__ __forceinline__ bool oets_desc(uint32_t k[4], int lane, int cap)
     return false;
 }
 
+// Odd-even transposition rounds on 128 64-bit keys (descending), as oets_desc.
+__device__ __forceinline__ bool oets_desc64(uint64_t k[4], int lane, int cap)
+{
+    for (int round = 0; round < cap; round++) {
+        bool moved = (k[0] < k[1]) || (k[2] < k[3]);
+        const uint64_t a0 = max(k[0], k[1]), a1 = min(k[0], k[1]);
+        const uint64_t a2 = max(k[2], k[3]), a3 = min(k[2], k[3]);
+        moved = moved || (a1 < a2);
+        k[1] = max(a1, a2);
+        k[2] = min(a1, a2);
+        const uint64_t nx = __shfl_down_sync(kFull, a0, 1);
+        const uint64_t pv = __shfl_up_sync(kFull, a3, 1);
+        moved = moved || (lane < 31 && a3 < nx);
+        k[3] = lane < 31 ? max(a3, nx) : a3;
+        k[0] = lane > 0 ? min(a0, pv) : a0;
+        if (!__any_sync(kFull, moved)) return true;
+    }
+    return false;
+}
+
 // Out of line: the exact-key sort for the rare rows whose quantized order fails.
 __device__ __noinline__ void sort_keys_exact(uint64_t key[4], int lane);
 
@@ -836,8 +856,10 @@ __device__ __noinline__ void sort_keys_exact(uint64_t key[4], int lane)
 
 // Steps 6-8 in exact arithmetic, for the rows the certified form cannot settle.
 // Lane l holds candidates 4l + e (token t_e, penalized logit l_e) in the
-// quantized order.  Exact probabilities make exact keys (sorted outright if the
-// quantized order breaks theirs); decisions come from exact f64 prefix sums
+// quantized order.  Exact probabilities make exact keys; where the quantized order
+// breaks theirs, odd-even rounds restore it (only neighbours within a quantum
+// are out of order), with a full sort after 8 rounds; decisions come from exact
+// f64 prefix sums
 // where the reference's margin allows, else term by term with the reference's
 // f32 sums.  The row's logits are no longer in shared memory: the next row's
 // copy may be landing there.  Returns the token in every lane.
@@ -867,7 +889,7 @@ __device__ __noinline__ int exact_decide(unsigned char *region, const double *ex
         const int i0 = 4 * lane;   // pairs (i, i + 1) with i + 1 < n_c
         const bool ok = (i0 + 1 >= n_c || key[0] > key[1]) && (i0 + 2 >= n_c || key[1] > key[2]) &&
                         (i0 + 3 >= n_c || key[2] > key[3]) && (i0 + 4 >= n_c || key[3] > nx);
-        if (!__all_sync(kFull, ok)) sort_keys_exact(key, lane);
+        if (!__all_sync(kFull, ok) && !oets_desc64(key, lane, 8)) sort_keys_exact(key, lane);
     }
     uint64_t *keys = reinterpret_cast<uint64_t *>(region + kKeysOffset);
     float *ps = reinterpret_cast<float *>(region + kPsOffset);
@@ -1213,6 +1235,9 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
             // bucket_bits = 0x4B000000 + b, so (bits * 4 + hbase) mod 2^32 is the
             // shared address of counter b
             const uint32_t hbase = smem_u32(hist) - 0x2C000000u;
+            // slots outside the counted buckets add to a word of their own lane (in
+            // the stage, unused until the scatter): the red needs no branch
+            const uint32_t spare = smem_u32(region + kStageOffset) + 4u * (uint32_t)lane;
             const float2 ns2 = make_float2(-s126, -s126), ms2 = make_float2(Ms126, Ms126);
             const float2 k2 = make_float2((float)(kBuckets - 2), (float)(kBuckets - 2));
             const float2 mag2 = make_float2(0x1p23f, 0x1p23f);
@@ -1228,10 +1253,11 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
                     bb[e + 1] = __float_as_uint(t.y);
                 }
 #pragma unroll
-                for (int e = 0; e < 4; e++)
-                    if (bb[e] < 0x4B000000u + (uint32_t)(kBuckets - 2))
-                        asm volatile("red.shared.add.u32 [%0], 1;" ::"r"(bb[e] * 4u + hbase)
-                                     : "memory");
+                for (int e = 0; e < 4; e++) {
+                    const uint32_t ad =
+                        bb[e] < 0x4B000000u + (uint32_t)(kBuckets - 2) ? bb[e] * 4u + hbase : spare;
+                    asm volatile("red.shared.add.u32 [%0], 1;" ::"r"(ad) : "memory");
+                }
                 bkt[lane + 32 * j] = __byte_perm(__byte_perm(bb[0], bb[1], 0x0040u),
                                                  __byte_perm(bb[2], bb[3], 0x0040u), 0x5410u);
             }
@@ -1250,18 +1276,9 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
             int bc = kBuckets - 2;   // every finite logit
             if (topk_on && n_fin > K) {
                 const int fl = __ffs(__ballot_sync(kFull, incl >= K)) - 1;
-                int bstar = 0;
-                if (lane == fl) {
-                    int c = incl - tot;
-#pragma unroll
-                    for (int i = 0; i < 4; i++) {
-                        c += h[i];
-                        if (c >= K) {
-                            bstar = 4 * lane + i;
-                            break;
-                        }
-                    }
-                }
+                // in lane fl: the first of its four buckets whose running count reaches K
+                const int c1 = incl - tot + h[0], c2 = c1 + h[1], c3 = c2 + h[2];
+                const int bstar = 4 * lane + (c1 < K) + (c2 < K) + (c3 < K);
                 bc = min(__shfl_sync(kFull, bstar, fl) + 1, kBuckets - 2);
             }
             int n_c;   // candidates: finite logits in buckets 0..bc
