@@ -80,7 +80,7 @@ SAMPLER_TRAFFIC_BYTES = 174.28e6
 LAUNCHES_PER_STEP = 1
 # Spin ahead of each timed region, so the host has queued the region's launches
 # before its start event fires (the first launch does not wait on the host).
-LEAD_CYCLES = 4_000_000
+LEAD_CYCLES = 1_000_000
 
 
 def dist_env():
