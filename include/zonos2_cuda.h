@@ -21,7 +21,7 @@
  *         context, and a later one with larger inputs (host-path staging,
  *         owned by the context);
  *       the first zonos2cu_sample_token on a device (a small per-device
- *         staging area, kept until exit);
+ *         staging area, device and page-locked host memory, kept until exit);
  *       zonos2cu_comm_create (NCCL's own buffers, freed by
  *         zonos2cu_comm_destroy).
  *     Every other entry point, zonos2cu_step_noalloc included, allocates
@@ -104,10 +104,12 @@ void zonos2cu_rng_seed(uint64_t seed, uint64_t state[4]);
  *                           float top_p, float min_p);
  * rng_state are the generator's four state words (host memory), advanced by
  * exactly one draw; logits are vocab_size host floats (1 <= vocab_size <=
- * 1024).  The row is sampled on the current CUDA device.  Equal
- * probabilities are taken in ascending token order.  Returns the token id,
- * or a negative ZONOS2CU_E* code (temp <= 0, NaN knobs, min_p > 1, or an
- * all-masked row -- the cases where the reference is undefined). */
+ * 1024).  The uniform is drawn on the host, as the reference draws it; the
+ * row is sampled on the current CUDA device (one copy in, one launch, one copy
+ * out).  Equal probabilities are taken in ascending token order.  Returns the
+ * token id, or a negative ZONOS2CU_E* code (temp <= 0, NaN knobs, min_p > 1,
+ * or an all-masked row -- the cases where the reference is undefined; the
+ * generator is left unadvanced when the arguments are rejected). */
 int zonos2cu_sample_token(uint64_t rng_state[4], const float *logits, int vocab_size,
                           float temp, int top_k, float top_p, float min_p);
 
@@ -192,7 +194,10 @@ int zonos2cu_set_allow(zonos2cu_ctx *ctx, const uint32_t *bits_host);
  * rms_norm_per_token(x, dim, n, eps, out_norm.weight) applied to the last hidden
  * states before the multi_output head (src/zonos2_model.cpp:684-685, :19-35).
  * With it enabled, ctx_step takes the un-normalised hidden states.  weight_host
- * is [dim] f32, or NULL for no scale weight; enable = 0 turns it off. */
+ * is [dim] f32, or NULL for no scale weight; enable = 0 turns it off.  With an
+ * f32 head the norm is the reference's, exactly; with a bf16 head it is folded
+ * into the head (the weight into W's columns, rounded to bf16 once; each row's
+ * 1 / rms into the GEMM's epilogue), within the bf16 path's tolerance. */
 int zonos2cu_set_out_norm(zonos2cu_ctx *ctx, int enable, const float *weight_host, float eps);
 /* Classifier-free guidance in zonos2cu_ctx_step: the blend
  * uncond + scale * (cond - uncond) of softcapped logits that the reference

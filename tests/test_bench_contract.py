@@ -80,7 +80,8 @@ def check_reference(d: dict) -> None:
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
 
 
-@pytest.mark.parametrize("name", ["bench_line_1gpu.json", "bench_line_2gpu.json"])
+@pytest.mark.parametrize("name", ["bench_line_1gpu.json", "bench_line_2gpu.json",
+                                  "bench_line_8gpu.json"])
 def test_kept_lines_keep_the_contract(name):
     path = os.path.join(REPO, "profiles", name)
     with open(path) as f:

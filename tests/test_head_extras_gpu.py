@@ -69,17 +69,21 @@ def test_out_norm_cfg_f32(z2, oracle, cuda, S, cfg):
     ctx.close()
 
 
-@pytest.mark.parametrize("S,cfg", [(128, 2.0), (256, None), (512, 1.5), (1024, 1.25)])
-def test_out_norm_cfg_bf16(z2, oracle, cuda, S, cfg):
+@pytest.mark.parametrize("S,cfg,weight", [(128, 2.0, True), (256, None, True), (512, 1.5, True),
+                                          (1024, 1.25, True), (64, None, False)])
+def test_out_norm_cfg_bf16(z2, oracle, cuda, S, cfg, weight):
     """bf16 tensor-core head: S=128 pairs and S=256 (256 hidden rows) on the
     one-SM kernel with 128-wide N tiles; 512 and 1024 pairs (1024 and 2048
     hidden rows) on the two-SM kernel, whose epilogue stores 16 blended output
-    rows per 32-row chunk."""
+    rows per 32-row chunk.  The bf16 head folds the norm: its weight scales W's
+    columns (rounded to bf16 once) and each row's 1 / rms multiplies the row's
+    dot products in the epilogue, so the logits are held to the stated bf16
+    tolerance against the oracle's f32 norm and head."""
     import torch
     rs = np.random.default_rng(9 + S)
     D = 2048
     Wb, Wf = _bf16(rs.normal(0, 0.02, size=(9 * 1024, D)).astype(np.float32))
-    gamma = rs.normal(1, 0.1, D).astype(np.float32)
+    gamma = rs.normal(1, 0.1, D).astype(np.float32) if weight else None
     rows = S * (2 if cfg else 1)
     hb, hf = _bf16(rs.normal(0, 4, (rows, D)).astype(np.float32))
     ctx = z2.Context(0, S, 9, 1024, D, 64, seed=7)
@@ -98,8 +102,10 @@ def test_out_norm_cfg_bf16(z2, oracle, cuda, S, cfg):
     got = logits.cpu().numpy()
     pick = np.unique(np.array([0, 1, S // 2, S - 1]))
     sub = np.sort(np.concatenate([2 * pick, 2 * pick + 1])) if cfg else pick
-    _, ref = _reference_logits(oracle, Wf, 1024, hf[sub], 1e-5, gamma, cfg, bf16_rows=True)
-    assert np.abs(got[pick] - ref).max() <= 1e-3      # stated bf16 tolerance: 2e-2
+    _, ref = _reference_logits(oracle, Wf, 1024, hf[sub], 1e-5, gamma, cfg)
+    err = np.abs(got[pick] - ref).max()
+    print(f"bf16 folded norm, S={S}: max |logit err| {err:.2e}")
+    assert err <= 2e-2                                 # stated bf16 tolerance
     prm = make_params(0.8, 50, 0.95, 0.02, 1.2, 1023)
     oc, _, _ = oracle.step(got, prm, oracle.rng_seed_streams(7, S), hist, hist_pos=0, exp_mode=1)
     assert (codes.cpu().numpy() == oc).all()

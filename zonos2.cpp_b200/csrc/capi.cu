@@ -131,14 +131,39 @@ cudaError_t dev_alloc(T **p, size_t n)
 }
 
 // ---- per-device staging for the sample_token drop-in --------------------
-struct Staging {   // each member is created on first use and kept until exit
+// One row per call: the uniform is drawn on the host from the caller's generator
+// (the reference's own draw), the row and its uniform go over in one copy from
+// page-locked memory, the sampler runs the row with that uniform (the decode
+// context's drawn-ahead path; the generator words it advances there are scratch),
+// and the code and flag come back in one copy.
+struct Staging {   // created on the first call on the device and kept until exit
     std::mutex mu;
+    bool ready = false;
     cudaStream_t stream = nullptr;
-    float *logits = nullptr;    // [1024]
-    uint64_t *rng = nullptr;    // [4]
-    int32_t *out = nullptr;     // [2] code, flag
+    float *h_in = nullptr;      // page-locked [1024] logits + [1] uniform
+    int32_t *h_out = nullptr;   // page-locked [2] code, flag
+    float *d_in = nullptr;      // [1024] logits, [1024] the uniform, [1025] scratch uniform
+    uint64_t *d_rng = nullptr;  // [8] scratch generator words
+    int32_t *d_out = nullptr;   // [2] code, flag
 };
 Staging g_staging[64];
+
+// The generator's next f32 uniform, as the reference draws it
+// (src/zonos2_generate.cpp:20-33): 53-bit double in [0, 1), narrowed to float.
+float host_randf(uint64_t st[4])
+{
+    const uint64_t s1 = st[1];
+    const uint64_t x = s1 * 5u;
+    const uint64_t out = ((x << 7) | (x >> 57)) * 9u;
+    const uint64_t t = st[1] << 17;
+    st[2] ^= st[0];
+    st[3] ^= st[1];
+    st[1] ^= st[2];
+    st[0] ^= st[3];
+    st[2] ^= t;
+    st[3] = (st[3] << 45) | (st[3] >> 19);
+    return (float)((double)(out >> 11) * 0x1.0p-53);
+}
 
 }  // namespace
 
@@ -213,31 +238,52 @@ int zonos2cu_sample_token(uint64_t rng_state[4], const float *logits, int vocab_
     if (dev < 0 || dev >= 64) return ZONOS2CU_EINVAL;
     Staging &st = g_staging[dev];
     std::lock_guard<std::mutex> lock(st.mu);
-    // first call on this device: a small staging area (a call that failed part way
+    // first call on this device: the staging area (a call that failed part way
     // keeps what it made, and the next one makes the rest)
-    if (!st.stream) {
-        cudaStream_t s = nullptr;
-        Z2_CK(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
-        st.stream = s;
+    if (!st.ready) {
+        if (!st.stream) {
+            cudaStream_t s = nullptr;
+            Z2_CK(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+            st.stream = s;
+        }
+        if (!st.h_in) {
+            void *h = nullptr;
+            Z2_CK(cudaHostAlloc(&h, sizeof(float) * (z2::kSamplerVocabMax + 4), cudaHostAllocDefault));
+            st.h_in = static_cast<float *>(h);
+        }
+        if (!st.h_out) {
+            void *h = nullptr;
+            Z2_CK(cudaHostAlloc(&h, sizeof(int32_t) * 2, cudaHostAllocDefault));
+            st.h_out = static_cast<int32_t *>(h);
+        }
+        if (!st.d_in) Z2_CK(dev_alloc(&st.d_in, z2::kSamplerVocabMax + 4));
+        if (!st.d_rng) {
+            Z2_CK(dev_alloc(&st.d_rng, 8));
+            Z2_CK(cudaMemsetAsync(st.d_rng, 0, sizeof(uint64_t) * 8, st.stream));
+        }
+        if (!st.d_out) Z2_CK(dev_alloc(&st.d_out, 2));
+        st.ready = true;
     }
-    if (!st.logits) Z2_CK(dev_alloc(&st.logits, z2::kSamplerVocabMax));
-    if (!st.rng) Z2_CK(dev_alloc(&st.rng, 4));
-    if (!st.out) Z2_CK(dev_alloc(&st.out, 2));
-    Z2_CK(cudaMemcpyAsync(st.logits, logits, sizeof(float) * vocab_size, cudaMemcpyHostToDevice,
-                          st.stream));
-    Z2_CK(cudaMemcpyAsync(st.rng, rng_state, sizeof(uint64_t) * 4, cudaMemcpyHostToDevice,
-                          st.stream));
-    rc = launch_rows(st.logits, 1, 1, vocab_size, vocab_size, &p, st.rng, nullptr, 0, 0, nullptr,
-                     -1, st.out, st.out + 1, st.stream);
-    if (rc) return rc;
-    int32_t out[2];
     uint64_t rs[4];
-    Z2_CK(cudaMemcpyAsync(out, st.out, sizeof(out), cudaMemcpyDeviceToHost, st.stream));
-    Z2_CK(cudaMemcpyAsync(rs, st.rng, sizeof(rs), cudaMemcpyDeviceToHost, st.stream));
+    memcpy(rs, rng_state, sizeof(rs));
+    const float u = host_randf(rs);   // the call's one draw
+    memcpy(st.h_in, logits, sizeof(float) * vocab_size);
+    st.h_in[z2::kSamplerVocabMax] = u;
+    // one copy: the row, then (past the row's vocab_size entries, which the sampler
+    // does not read) the uniform at entry 1024
+    Z2_CK(cudaMemcpyAsync(st.d_in, st.h_in, sizeof(float) * (z2::kSamplerVocabMax + 1),
+                          cudaMemcpyHostToDevice, st.stream));
+    rc = launch_rows(st.d_in, 1, 1, vocab_size, vocab_size, &p, st.d_rng, nullptr, 0, 0, nullptr,
+                     -1, st.d_out, st.d_out + 1, st.stream, nullptr, nullptr, false,
+                     st.d_in + z2::kSamplerVocabMax, st.d_in + z2::kSamplerVocabMax + 1,
+                     st.d_rng + 4);
+    if (rc) return rc;
+    Z2_CK(cudaMemcpyAsync(st.h_out, st.d_out, sizeof(int32_t) * 2, cudaMemcpyDeviceToHost,
+                          st.stream));
     Z2_CK(cudaStreamSynchronize(st.stream));
     memcpy(rng_state, rs, sizeof(rs));
-    if (out[1] & ZONOS2CU_FLAG_ALL_MASKED) return ZONOS2CU_EINVAL;
-    return out[0];
+    if (st.h_out[1] & ZONOS2CU_FLAG_ALL_MASKED) return ZONOS2CU_EINVAL;
+    return st.h_out[0];
 }
 
 }  // extern "C"
@@ -259,7 +305,7 @@ int check_head(const void *W_dev, zonos2cu_dtype dtype, int rows_per_cb, int n_c
 // batch / 2 blended rows.
 int launch_head(const void *W_dev, zonos2cu_dtype dtype, int rows_per_cb, int n_cb, int vocab,
                 int dim, const void *hidden_dev, int batch, float softcap, float *logits_dev,
-                void *stream, bool cfg, float cfg_scale)
+                void *stream, bool cfg, float cfg_scale, const float *row_scale = nullptr)
 {
     int rc = check_head(W_dev, dtype, rows_per_cb, n_cb, vocab, dim, hidden_dev, batch, softcap,
                         logits_dev);
@@ -267,6 +313,7 @@ int launch_head(const void *W_dev, zonos2cu_dtype dtype, int rows_per_cb, int n_
     z2::HeadArgs a{W_dev, rows_per_cb, n_cb, vocab, dim, hidden_dev, batch, softcap, logits_dev};
     a.cfg = cfg ? 1 : 0;
     a.cfg_scale = cfg_scale;
+    a.row_scale = row_scale;
     cudaError_t e;
     if (dtype == ZONOS2CU_F32) {
         e = z2::launch_head_gemv_f32(a, (cudaStream_t)stream);
@@ -377,7 +424,9 @@ struct zonos2cu_ctx {
     float norm_eps = 1e-5f;
     float *norm_w = nullptr;     // [D] or unused
     bool norm_has_w = false;
-    void *normed = nullptr;      // [2S][D] of the head's type: the normalised rows
+    void *normed = nullptr;      // [2S][D] f32: the normalised rows (f32 head)
+    void *head_folded = nullptr; // bf16 head with the norm weight folded into its columns
+    float *row_rcp = nullptr;    // [2S]: 1 / rms of each hidden row (bf16 head)
     // classifier-free guidance (zonos2cu_set_cfg): steps take 2S hidden rows
     bool cfg_on = false;
     float cfg_scale = 1.0f;
@@ -425,6 +474,20 @@ int grow(void **p, size_t *cap, size_t want)
     *cap = 0;
     Z2_CK(cudaMalloc(p, want));
     *cap = want;
+    return ZONOS2CU_OK;
+}
+
+// The bf16 head with the output norm's weight folded into its columns, when both
+// are set (synchronises the context's stream).
+int refold_head(zonos2cu_ctx *c)
+{
+    if (!c->norm_on || !c->norm_has_w || !c->head || c->head_dtype != ZONOS2CU_BF16)
+        return ZONOS2CU_OK;
+    const size_t rows = (size_t)c->dims.n_cb * c->dims.vocab, D = (size_t)c->dims.dim;
+    if (!c->head_folded) Z2_CK(cudaMalloc(&c->head_folded, 2 * rows * D));
+    Z2_CK(z2::launch_fold_columns(c->head, c->norm_w, (int)rows, (int)D, c->head_folded,
+                                  c->stream));
+    Z2_CK(cudaStreamSynchronize(c->stream));
     return ZONOS2CU_OK;
 }
 
@@ -513,6 +576,8 @@ int zonos2cu_ctx_destroy(zonos2cu_ctx *c)
     cudaFree(c->logits);
     cudaFree(c->norm_w);
     cudaFree(c->normed);
+    cudaFree(c->head_folded);
+    cudaFree(c->row_rcp);
     cudaFree(c->gen_frames);
     cudaFree(c->gen_count);
     cudaFree(c->gen_next);
@@ -549,7 +614,9 @@ int zonos2cu_set_head(zonos2cu_ctx *c, const void *W_host, zonos2cu_dtype dtype,
     Z2_CK(cudaStreamSynchronize(c->stream));
     c->head_dtype = dtype;
     if (!c->logits && n_rows(c)) Z2_CK(cudaMalloc(&c->logits, sizeof(float) * n_rows(c) * V));
-    return ZONOS2CU_OK;
+    if (c->norm_on && dtype == ZONOS2CU_F32 && !c->normed && n_rows(c))
+        Z2_CK(cudaMalloc(&c->normed, sizeof(float) * 2 * (size_t)c->dims.n_streams * c->dims.dim));
+    return refold_head(c);
 }
 
 int zonos2cu_set_history(zonos2cu_ctx *c, const int32_t *hist_host, int hist_pos)
@@ -648,8 +715,12 @@ int zonos2cu_set_out_norm(zonos2cu_ctx *c, int enable, const float *weight_host,
         return ZONOS2CU_OK;
     }
     const size_t D = (size_t)c->dims.dim;
-    if (!c->normed && n_rows(c))   // room for 2S rows of f32 covers every mode
-        Z2_CK(cudaMalloc(&c->normed, sizeof(float) * 2 * (size_t)c->dims.n_streams * D));
+    const size_t S2 = 2 * (size_t)c->dims.n_streams;   // rows with guidance on
+    // the f32 head normalises into a copy (room for 2S rows covers every mode);
+    // the bf16 head takes the rows' 1 / rms and, with a weight, a folded head
+    if (!c->normed && n_rows(c) && (!c->head || c->head_dtype == ZONOS2CU_F32))
+        Z2_CK(cudaMalloc(&c->normed, sizeof(float) * S2 * D));
+    if (!c->row_rcp && n_rows(c)) Z2_CK(cudaMalloc(&c->row_rcp, sizeof(float) * S2));
     if (weight_host) {
         if (!c->norm_w) Z2_CK(cudaMalloc(&c->norm_w, sizeof(float) * D));
         Z2_CK(cudaMemcpyAsync(c->norm_w, weight_host, sizeof(float) * D, cudaMemcpyHostToDevice,
@@ -659,7 +730,7 @@ int zonos2cu_set_out_norm(zonos2cu_ctx *c, int enable, const float *weight_host,
     c->norm_has_w = weight_host != nullptr;
     c->norm_eps = eps;
     c->norm_on = true;
-    return ZONOS2CU_OK;
+    return refold_head(c);
 }
 
 int zonos2cu_set_cfg(zonos2cu_ctx *c, int enable, float scale)
@@ -870,13 +941,21 @@ int zonos2cu_ctx_step(zonos2cu_ctx *c, const void *hidden_dev, zonos2cu_dtype dt
     float *lg = logits_out_dev ? logits_out_dev : c->logits;
     const int rows_in = (c->cfg_on ? 2 : 1) * d.n_streams;
     const void *h = hidden_dev;
+    const void *W = c->head;
+    const float *row_scale = nullptr;
     if (c->norm_on && rows_in > 0) {   // rms_norm_per_token (src/zonos2_model.cpp:684-685)
-        Z2_CK(z2::launch_out_norm(hidden_dev, dtype == ZONOS2CU_BF16, rows_in, d.dim, c->norm_eps,
-                                  c->norm_has_w ? c->norm_w : nullptr, c->normed, st));
-        h = c->normed;
+        if (dtype == ZONOS2CU_BF16) {   // folded: the weight in W's columns, 1 / rms per row
+            Z2_CK(z2::launch_row_rcp_rms(hidden_dev, rows_in, d.dim, c->norm_eps, c->row_rcp, st));
+            if (c->norm_has_w) W = c->head_folded;
+            row_scale = c->row_rcp;
+        } else {                        // the exact restatement into a normalised copy
+            Z2_CK(z2::launch_out_norm(hidden_dev, false, rows_in, d.dim, c->norm_eps,
+                                      c->norm_has_w ? c->norm_w : nullptr, c->normed, st));
+            h = c->normed;
+        }
     }
-    rc = launch_head(c->head, dtype, d.vocab, d.n_cb, d.vocab, d.dim, h, rows_in, 15.0f, lg, st,
-                     c->cfg_on, c->cfg_scale);
+    rc = launch_head(W, dtype, d.vocab, d.n_cb, d.vocab, d.dim, h, rows_in, 15.0f, lg, st,
+                     c->cfg_on, c->cfg_scale, row_scale);
     if (rc) return rc;
     return zonos2cu_ctx_sample(c, lg, d.vocab, params, delay_step, codes_dev, flags_dev, st);
 }

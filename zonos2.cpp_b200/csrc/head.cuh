@@ -18,6 +18,10 @@ struct HeadArgs {
     // softcapped rows (src/zonos2_generate.cpp:178-183).  batch is even.
     int cfg = 0;
     float cfg_scale = 1.0f;
+    // Per hidden row, a factor applied to the row's dot products before the
+    // softcap (bf16 kernel only): the output RMSNorm's 1 / rms when its weight has
+    // been folded into the columns of W.  nullptr: none.
+    const float *row_scale = nullptr;
 };
 
 // The output RMSNorm of rows x [rows][dim] (f32, or bf16 when `bf16`) into y of
@@ -25,6 +29,17 @@ struct HeadArgs {
 // (head_prologue.cu).
 cudaError_t launch_out_norm(const void *x, bool bf16, int rows, int dim, float eps,
                             const float *w, void *y, cudaStream_t stream);
+
+// 1 / rms of each row of x [rows][dim] (bf16), rms = sqrt(mean of squares + eps),
+// into rcp [rows] f32: the output RMSNorm's row factor, applied by the bf16 head's
+// epilogue when the norm's weight is folded into W (head_prologue.cu).
+cudaError_t launch_row_rcp_rms(const void *x, int rows, int dim, float eps, float *rcp,
+                               cudaStream_t stream);
+
+// W'[r][k] = bf16(W[r][k] * w[k]) for rows x dim bf16 W and f32 w: the output
+// RMSNorm's weight folded into the columns of the head (head_prologue.cu).
+cudaError_t launch_fold_columns(const void *W, const float *w, int rows, int dim, void *out,
+                                cudaStream_t stream);
 
 // f32 weights and hidden states: one warp per output row, f64 accumulation
 // (head_gemv.cu).

@@ -8,7 +8,11 @@
 // order (the other lanes have nothing to add without changing its rounding),
 // then the warp writes the normalised row.  Built with -fmad=false, so every
 // operation rounds where the reference's does; bf16 rows are widened to f32
-// first and the result is rounded back to bf16 for the tensor-core head.
+// first and the result is rounded back to bf16 for the tensor-core head when
+// the norm has no weight to fold.  With a weight, the bf16 head takes the
+// weight folded into its columns (fold_columns_kernel, once) and the rows'
+// 1 / rms (row_rcp_rms_kernel, per step) in its epilogue: no normalised copy of
+// the hidden states is written or read.
 #include <cuda_bf16.h>
 #include <math.h>
 
@@ -65,7 +69,71 @@ __global__ void __launch_bounds__(32 * kNormWarps)
     }
 }
 
+// One warp per bf16 row: the sum of squares (lanes take eight elements at a
+// time, then a shuffle tree; the bf16 path is held to its stated tolerance,
+// not to the reference's order of additions), rms = sqrt(ss / dim + eps),
+// rcp = 1 / rms.
+__global__ void __launch_bounds__(32 * kNormWarps)
+    row_rcp_rms_kernel(const __nv_bfloat16 *__restrict__ x, int rows, int dim, float eps,
+                       float *__restrict__ rcp)
+{
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * kNormWarps + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const __nv_bfloat16 *xr = x + (size_t)row * dim;
+    float ss = 0.0f;
+    if (dim % 8 == 0 && ((uintptr_t)xr & 15u) == 0) {
+        for (int d = 8 * lane; d < dim; d += 256) {
+            const uint4 v = __ldg(reinterpret_cast<const uint4 *>(xr + d));
+            const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const float a = __uint_as_float(w4[k] << 16), b = __uint_as_float(w4[k] & 0xffff0000u);
+                ss = __fadd_rn(ss, __fadd_rn(__fmul_rn(a, a), __fmul_rn(b, b)));
+            }
+        }
+    } else {
+        for (int d = lane; d < dim; d += 32) {
+            const float a = __bfloat162float(xr[d]);
+            ss = __fadd_rn(ss, __fmul_rn(a, a));
+        }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(kFull, ss, o));
+    if (lane == 0) rcp[row] = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)dim), eps)));
+}
+
+// W'[r][k] = bf16(W[r][k] * w[k]), one thread per element.
+__global__ void fold_columns_kernel(const __nv_bfloat16 *__restrict__ W, const float *__restrict__ w,
+                                    long long n, int dim, __nv_bfloat16 *__restrict__ out)
+{
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int k = (int)(i % dim);
+    out[i] = __float2bfloat16_rn(__fmul_rn(__bfloat162float(W[i]), __ldg(w + k)));
+}
+
 }  // namespace
+
+cudaError_t launch_row_rcp_rms(const void *x, int rows, int dim, float eps, float *rcp,
+                               cudaStream_t stream)
+{
+    if (rows == 0) return cudaSuccess;
+    const unsigned blocks = (unsigned)((rows + kNormWarps - 1) / kNormWarps);
+    row_rcp_rms_kernel<<<blocks, 32 * kNormWarps, 0, stream>>>(
+        static_cast<const __nv_bfloat16 *>(x), rows, dim, eps, rcp);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_fold_columns(const void *W, const float *w, int rows, int dim, void *out,
+                                cudaStream_t stream)
+{
+    const long long n = (long long)rows * dim;
+    if (n == 0) return cudaSuccess;
+    fold_columns_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16 *>(W), w, n, dim, static_cast<__nv_bfloat16 *>(out));
+    return cudaGetLastError();
+}
 
 cudaError_t launch_out_norm(const void *x, bool bf16, int rows, int dim, float eps,
                             const float *w, void *y, cudaStream_t stream)

@@ -198,7 +198,14 @@ struct TcArgs {
     int cfg;     // rows 2s, 2s+1 (conditional, unconditional) blend into out row s
     float cfg_scale;
     int out_rows;   // rows of out: batch, or batch / 2 with cfg
+    const float *row_scale;   // [batch] factor per hidden row before the softcap, or nullptr
 };
+
+// The factor of hidden row `row` (1 when there is none or the row is past the batch).
+__device__ __forceinline__ float row_factor(const TcArgs &args, int row)
+{
+    return args.row_scale && row < args.batch ? __ldg(args.row_scale + row) : 1.0f;
+}
 
 // The epilogue's 32 output values of one 32-column chunk of this lane's row
 // (rows 2s and 2s+1 sit in neighbouring lanes of one warp): the softcap, and
@@ -206,12 +213,12 @@ struct TcArgs {
 // from the neighbouring lane; the even lane's values are output row s
 // (src/zonos2_generate.cpp:178-183).  Every lane takes part.
 __device__ __forceinline__ void finish_chunk(const TcArgs &args, const uint32_t (&r)[32], float k2,
-                                             float (&o)[32])
+                                             float rsc, float (&o)[32])
 {
     const float cap = args.softcap;
 #pragma unroll
     for (int i = 0; i < 32; i++) {
-        const float l = __uint_as_float(r[i]);
+        const float l = args.row_scale ? __uint_as_float(r[i]) * rsc : __uint_as_float(r[i]);
         o[i] = cap > 0.0f ? softcap_fast(l, cap, k2) : l;
         if (args.cfg) {
             const float u = __shfl_xor_sync(kFull, o[i], 1);
@@ -383,13 +390,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int mt = tile % args.tiles_m, nt = tile / args.tiles_m;
             const int row0 = mt * kBM + 32 * q;
             const int y0 = args.cfg ? row0 >> 1 : row0;
+            const float rsc = row_factor(args, row0 + lane);   // this lane's hidden row
             const float k2 = 2.0f * 1.4426950408889634f / args.softcap;   // 2 log2(e) / cap
 #pragma unroll 1
             for (int ch = half * (BN / 64); ch < (half + 1) * (BN / 64); ch++) {
                 uint32_t r[32];
                 tmem_ld32(tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BN + 32 * ch), r);
                 float o[32];
-                finish_chunk(args, r, k2, o);
+                finish_chunk(args, r, k2, rsc, o);
                 if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
                 __syncwarp();
                 if (owner) {
@@ -694,13 +702,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const int mt = tile % tiles_m2, nt = tile / tiles_m2;
             const int row0 = mt * 2 * kBM + (int)rank * kBM + 32 * q;   // the warp's first row
             const int y0 = args.cfg ? row0 >> 1 : row0;                  // its first output row
+            const float rsc = row_factor(args, row0 + lane);            // this lane's hidden row
             const float k2 = 2.0f * 1.4426950408889634f / args.softcap;   // 2 log2(e) / cap
 #pragma unroll 1
             for (int ch = half * (BN / 64); ch < (half + 1) * (BN / 64); ch++) {
                 uint32_t r[32];
                 tmem_ld32(tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BN + 32 * ch), r);
                 float o[32];
-                finish_chunk(args, r, k2, o);
+                finish_chunk(args, r, k2, rsc, o);
                 if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
                 __syncwarp();   // the previous chunk has left the staging buffer
                 if (owner) {
@@ -854,6 +863,7 @@ cudaError_t launch_pair(const HeadArgs &a, const CUtensorMap &ma, int tiles_m, i
     t.cfg = a.cfg;
     t.cfg_scale = a.cfg_scale;
     t.out_rows = a.cfg ? a.batch / 2 : a.batch;
+    t.row_scale = a.row_scale;
     CUtensorMap mo;   // the logits, f32, 32 x 32 chunks (16 output rows with guidance)
     if (!make_map_f32(&mo, a.out, (uint64_t)t.out_rows, (uint64_t)a.n_cb * a.vocab,
                       a.cfg ? 16 : 32))
@@ -901,6 +911,7 @@ cudaError_t launch_bn(const HeadArgs &a, const CUtensorMap &ma, int tiles_m, int
     t.cfg = a.cfg;
     t.cfg_scale = a.cfg_scale;
     t.out_rows = a.cfg ? a.batch / 2 : a.batch;
+    t.row_scale = a.row_scale;
     CUtensorMap mo;
     if (!make_map_f32(&mo, a.out, (uint64_t)t.out_rows, (uint64_t)a.n_cb * a.vocab,
                       a.cfg ? 16 : 32))
