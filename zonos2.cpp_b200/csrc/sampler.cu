@@ -1044,6 +1044,14 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
     item_at(blockIdx.x + (long long)gridDim.x * w, s, cb);
 
     uint32_t phase = 0u;
+    // The warp's first row towards L2 while the kernel before this one finishes: a
+    // prefetch reads nothing into the CTA, and L2 holds every write that kernel
+    // makes, so it is safe whatever that kernel writes.
+    if (a.vec_logits && lane == 0 && cb < NCB)
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(
+                         a.logits + ((long long)s * NCB + cb) * a.row_stride),
+                     "r"(row_bytes)
+                     : "memory");
     // With uniforms drawn ahead the kernel before this one may be the previous
     // step's sampler (history index, generators) or the head (logits): wait for it
     // before any global read.  Either way the next launch may be scheduled now.
