@@ -282,8 +282,21 @@ def measure_drop_in(Z, frames: int = 20):
         for cb in range(NCB):
             Z.sample_token(rng, rows[2 + f, cb], 1024, 0.7, 50, 0.9, 0.02)
     dt = time.perf_counter() - t0
+    # the same frames as one call each through a one-stream context (9 codebooks,
+    # the same generator, the reference's [9][1026] layout)
+    ctx = Z.Context(0, 1, NCB, VOCAB, 0, 0, seed=42)
+    params = Z.SampleParams(0.7, 50, 0.9, 0.02, 1.0, PAD)
+    codes = np.zeros((1, NCB), np.int32)
+    ctx.sample_host(rows[0:1], params, codes, row_stride=1026)
+    t1 = time.perf_counter()
+    for f in range(frames):
+        ctx.sample_host(rows[2 + f:3 + f], params, codes, row_stride=1026)
+    dt_ctx = time.perf_counter() - t1
+    ctx.close()
     return {"us_per_call": dt / (frames * NCB) * 1e6, "us_per_frame": dt / frames * 1e6,
-            "frames": frames}
+            "frames": frames, "context_us_per_frame": dt_ctx / frames * 1e6,
+            "what": "zonos2cu_sample_token, 9 calls per frame; and one zonos2cu_ctx_sample_host "
+                    "call per frame on a one-stream context"}
 
 
 def run_head_only(args):
