@@ -1208,8 +1208,9 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
                 mx = careful_prologue(rowf, lane, V, seenm, allowm, validm, a.rho, a.inv_rho, v,
                                       &km, &nonfin);
         }
-#pragma unroll
-        for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+        // the warp's max in one instruction (sm_100a; a max, so exact); mx is never
+        // NaN here (non-finite rows took the careful prologue)
+        asm("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(mx) : "f"(mx));
         const bool live = mx >= -1e9f;  // running max starts at -1e9: :41-42
         const int flag = (__any_sync(kFull, nonfin) ? 2 : 0) | (live ? 0 : 1);
         // The evicted token leaves the history index now that the row's set has been
