@@ -134,17 +134,18 @@ cudaError_t dev_alloc(T **p, size_t n)
 // One row per call: the uniform is drawn on the host from the caller's generator
 // (the reference's own draw), the row and its uniform go over in one copy from
 // page-locked memory, the sampler runs the row with that uniform (the decode
-// context's drawn-ahead path; the generator words it advances there are scratch),
-// and the code and flag come back in one copy.
+// context's drawn-ahead path; the generator words it advances there are scratch)
+// and writes the code and flag straight into mapped page-locked memory, so no
+// copy comes back.
 struct Staging {   // created on the first call on the device and kept until exit
     std::mutex mu;
     bool ready = false;
     cudaStream_t stream = nullptr;
     float *h_in = nullptr;      // page-locked [1024] logits + [1] uniform
-    int32_t *h_out = nullptr;   // page-locked [2] code, flag
+    int32_t *h_out = nullptr;   // page-locked and mapped [2] code, flag
+    int32_t *h_out_dev = nullptr;   // h_out as the device sees it
     float *d_in = nullptr;      // [1024] logits, [1024] the uniform, [1025] scratch uniform
     uint64_t *d_rng = nullptr;  // [8] scratch generator words
-    int32_t *d_out = nullptr;   // [2] code, flag
 };
 Staging g_staging[64];
 
@@ -253,15 +254,19 @@ int zonos2cu_sample_token(uint64_t rng_state[4], const float *logits, int vocab_
         }
         if (!st.h_out) {
             void *h = nullptr;
-            Z2_CK(cudaHostAlloc(&h, sizeof(int32_t) * 2, cudaHostAllocDefault));
+            Z2_CK(cudaHostAlloc(&h, sizeof(int32_t) * 2, cudaHostAllocMapped));
             st.h_out = static_cast<int32_t *>(h);
+        }
+        if (!st.h_out_dev) {
+            void *d = nullptr;
+            Z2_CK(cudaHostGetDevicePointer(&d, st.h_out, 0));
+            st.h_out_dev = static_cast<int32_t *>(d);
         }
         if (!st.d_in) Z2_CK(dev_alloc(&st.d_in, z2::kSamplerVocabMax + 4));
         if (!st.d_rng) {
             Z2_CK(dev_alloc(&st.d_rng, 8));
             Z2_CK(cudaMemsetAsync(st.d_rng, 0, sizeof(uint64_t) * 8, st.stream));
         }
-        if (!st.d_out) Z2_CK(dev_alloc(&st.d_out, 2));
         st.ready = true;
     }
     uint64_t rs[4];
@@ -274,13 +279,11 @@ int zonos2cu_sample_token(uint64_t rng_state[4], const float *logits, int vocab_
     Z2_CK(cudaMemcpyAsync(st.d_in, st.h_in, sizeof(float) * (z2::kSamplerVocabMax + 1),
                           cudaMemcpyHostToDevice, st.stream));
     rc = launch_rows(st.d_in, 1, 1, vocab_size, vocab_size, &p, st.d_rng, nullptr, 0, 0, nullptr,
-                     -1, st.d_out, st.d_out + 1, st.stream, nullptr, nullptr, false,
+                     -1, st.h_out_dev, st.h_out_dev + 1, st.stream, nullptr, nullptr, false,
                      st.d_in + z2::kSamplerVocabMax, st.d_in + z2::kSamplerVocabMax + 1,
                      st.d_rng + 4);
     if (rc) return rc;
-    Z2_CK(cudaMemcpyAsync(st.h_out, st.d_out, sizeof(int32_t) * 2, cudaMemcpyDeviceToHost,
-                          st.stream));
-    Z2_CK(cudaStreamSynchronize(st.stream));
+    Z2_CK(cudaStreamSynchronize(st.stream));   // the code and flag are in h_out
     memcpy(rng_state, rs, sizeof(rs));
     if (st.h_out[1] & ZONOS2CU_FLAG_ALL_MASKED) return ZONOS2CU_EINVAL;
     return st.h_out[0];
