@@ -449,7 +449,8 @@ struct zonos2cu_ctx {
     size_t in_logits_bytes = 0;
     void *in_hidden = nullptr;
     size_t in_hidden_bytes = 0;
-    int32_t *out = nullptr;      // [2][S][C] codes, flags
+    int32_t *out = nullptr;      // [2][S][C] codes, flags, as the device writes them
+    int32_t *out_host = nullptr; // the same memory, page-locked and mapped, for small batches
 };
 
 namespace {
@@ -494,10 +495,48 @@ int refold_head(zonos2cu_ctx *c)
     return ZONOS2CU_OK;
 }
 
+// Small batches: the host path's codes and flags are written by the kernels
+// straight into mapped page-locked memory, so no copy comes back (a frame of a
+// one-stream context, 45 -> 35 us per call).  Larger batches copy them back in
+// one piece each, which beats that many scattered writes over PCIe.
+constexpr size_t kMappedOutRows = 2304;
+
 int ensure_out(zonos2cu_ctx *c)
 {
     if (c->out) return ZONOS2CU_OK;
-    Z2_CK(cudaMalloc(&c->out, sizeof(int32_t) * 2 * (n_rows(c) ? n_rows(c) : 1)));
+    const size_t n = 2 * (n_rows(c) ? n_rows(c) : 1);
+    if (n_rows(c) <= kMappedOutRows) {
+        void *h = nullptr, *d = nullptr;
+        Z2_CK(cudaHostAlloc(&h, sizeof(int32_t) * n, cudaHostAllocMapped));
+        const cudaError_t e = cudaHostGetDevicePointer(&d, h, 0);
+        if (e != cudaSuccess) {
+            cudaFreeHost(h);
+            return cuda_fail(e, "mapped output");
+        }
+        c->out_host = static_cast<int32_t *>(h);
+        c->out = static_cast<int32_t *>(d);
+        return ZONOS2CU_OK;
+    }
+    Z2_CK(cudaMalloc(&c->out, sizeof(int32_t) * n));
+    return ZONOS2CU_OK;
+}
+
+// The host path's codes (and flags) of the step just enqueued on c->stream, on
+// the host when it returns.
+int finish_host_step(zonos2cu_ctx *c, size_t rows, int32_t *codes_host, int32_t *flags_host)
+{
+    if (c->out_host) {
+        Z2_CK(cudaStreamSynchronize(c->stream));
+        memcpy(codes_host, c->out_host, sizeof(int32_t) * rows);
+        if (flags_host) memcpy(flags_host, c->out_host + rows, sizeof(int32_t) * rows);
+        return ZONOS2CU_OK;
+    }
+    Z2_CK(cudaMemcpyAsync(codes_host, c->out, sizeof(int32_t) * rows, cudaMemcpyDeviceToHost,
+                          c->stream));
+    if (flags_host)
+        Z2_CK(cudaMemcpyAsync(flags_host, c->out + rows, sizeof(int32_t) * rows,
+                              cudaMemcpyDeviceToHost, c->stream));
+    Z2_CK(cudaStreamSynchronize(c->stream));
     return ZONOS2CU_OK;
 }
 
@@ -588,7 +627,10 @@ int zonos2cu_ctx_destroy(zonos2cu_ctx *c)
     cudaFree(c->emb_text);
     cudaFree(c->in_logits);
     cudaFree(c->in_hidden);
-    cudaFree(c->out);
+    if (c->out_host)
+        cudaFreeHost(c->out_host);
+    else
+        cudaFree(c->out);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
     return ZONOS2CU_OK;
@@ -920,13 +962,7 @@ int zonos2cu_ctx_sample_host(zonos2cu_ctx *c, const float *logits_host, long lon
     rc = zonos2cu_ctx_sample(c, c->in_logits, row_stride, params, delay_step, c->out,
                              c->out + rows, c->stream);
     if (rc) return rc;
-    Z2_CK(cudaMemcpyAsync(codes_host, c->out, sizeof(int32_t) * rows, cudaMemcpyDeviceToHost,
-                          c->stream));
-    if (flags_host)
-        Z2_CK(cudaMemcpyAsync(flags_host, c->out + rows, sizeof(int32_t) * rows,
-                              cudaMemcpyDeviceToHost, c->stream));
-    Z2_CK(cudaStreamSynchronize(c->stream));
-    return ZONOS2CU_OK;
+    return finish_host_step(c, rows, codes_host, flags_host);
 }
 
 int zonos2cu_ctx_step(zonos2cu_ctx *c, const void *hidden_dev, zonos2cu_dtype dtype,
@@ -981,13 +1017,7 @@ int zonos2cu_ctx_step_host(zonos2cu_ctx *c, const void *hidden_host, zonos2cu_dt
     rc = zonos2cu_ctx_step(c, c->in_hidden, dtype, params, delay_step, c->out, c->out + rows,
                            nullptr, c->stream);
     if (rc) return rc;
-    Z2_CK(cudaMemcpyAsync(codes_host, c->out, sizeof(int32_t) * rows, cudaMemcpyDeviceToHost,
-                          c->stream));
-    if (flags_host)
-        Z2_CK(cudaMemcpyAsync(flags_host, c->out + rows, sizeof(int32_t) * rows,
-                              cudaMemcpyDeviceToHost, c->stream));
-    Z2_CK(cudaStreamSynchronize(c->stream));
-    return ZONOS2CU_OK;
+    return finish_host_step(c, rows, codes_host, flags_host);
 }
 
 }  // extern "C"
