@@ -305,7 +305,20 @@ int zonos2cu_shard_range(long long n_streams, int n_ranks, int rank, long long *
 int zonos2cu_comm_unique_id(unsigned char id[128]);
 int zonos2cu_comm_create(int device, int n_ranks, int rank, const unsigned char id[128],
                          void **nccl_comm_out);
+/* The same communicator, set up without blocking (ncclCommInitRankConfig with
+ * blocking = 0) and polled: if every rank has not joined within timeout_ms the
+ * set-up is aborted (ncclCommAbort) and ZONOS2CU_ENCCL returned, so a rank that
+ * died or never started cannot hang the others in set-up.  Its gathers wait at
+ * most 120 s for connections and its destroy at most 60 s for the flush (then
+ * aborts).  Needs NCCL >= 2.14; otherwise ZONOS2CU_ENCCL. */
+int zonos2cu_comm_create_timeout(int device, int n_ranks, int rank, const unsigned char id[128],
+                                 int timeout_ms, void **nccl_comm_out);
+/* Flushes (a communicator from zonos2cu_comm_create_timeout, within 60 s) and
+ * frees a communicator. */
 int zonos2cu_comm_destroy(void *nccl_comm);
+/* Frees a communicator at once, ending the operations still in flight on it
+ * (ncclCommAbort): the error path when a peer rank is known to be gone. */
+int zonos2cu_comm_abort(void *nccl_comm);
 /* Collects n_steps steps of codes on rank `root`, called by every rank of the
  * communicator with the same root, n_steps, n_streams (the global batch) and
  * n_cb, on `stream` (asynchronous; nothing is synchronised).  codes_dev is this

@@ -93,3 +93,62 @@ def test_fused_step_rollout(z2, oracle, cuda, S, norm, allow, knobs):
     assert hp == pos and (hh == hist).all()
     assert z2.device_error() == 0
     ctx.close()
+
+
+def test_context_checkpoint_and_resume(z2, oracle, cuda):
+    """The decode state (generators, history ring and position) read from one
+    context mid-rollout and written into a fresh one: both continue with the
+    same codes (and the same state) as the uninterrupted rollout."""
+    import torch
+    import workloads as W
+    cfg = W.CONFIGS[4]
+    S, Cb = 64, 9
+    p = z2.SampleParams(cfg.temperature, cfg.top_k, cfg.top_p, cfg.min_p, cfg.penalty, W.PAD)
+    a = z2.Context(0, S, Cb, 1024, 0, cfg.hist_len, seed=cfg.seed)
+    a.set_history(W.initial_history(cfg, S), 0)
+    a.set_allow(W.allow_bits(cfg, S))
+    codes_a = torch.zeros((S, Cb), dtype=torch.int32, device=cuda)
+    codes_b = torch.zeros((S, Cb), dtype=torch.int32, device=cuda)
+    for step in range(3):
+        a.sample(_t(W.step_logits(cfg, step, S), cuda), p, codes_a, delay_step=step)
+    torch.cuda.synchronize()
+    rng, (hist, pos) = a.get_rng(), a.get_history()
+    b = z2.Context(0, S, Cb, 1024, 0, cfg.hist_len, seed=12345)   # another seed: overwritten
+    b.set_history(hist, pos)
+    b.set_rng(rng)
+    b.set_allow(W.allow_bits(cfg, S))
+    for step in range(3, 9):
+        lg = _t(W.step_logits(cfg, step, S), cuda)
+        a.sample(lg, p, codes_a, delay_step=step)
+        b.sample(lg, p, codes_b, delay_step=step)
+        torch.cuda.synchronize()
+        assert torch.equal(codes_a, codes_b), step
+    assert (a.get_rng() == b.get_rng()).all()
+    ha, pa = a.get_history()
+    hb, pb = b.get_history()
+    assert pa == pb and (ha == hb).all()
+    a.close()
+    b.close()
+
+
+def test_failed_allocation_is_reported_and_leaves_the_device_usable(z2, oracle, cuda):
+    """A context whose history ring cannot fit (2^20 streams x 16 codebooks x
+    65535 entries: 4.4 TB) is refused with ZONOS2CU_ENOMEM after the buffers it
+    did get are freed; the next context on the same thread samples normally
+    (the refused allocation's error is not left for the next launch to find)."""
+    import torch
+    with pytest.raises(z2.Zonos2cuError) as e:
+        z2.Context(0, 1 << 20, 16, 1024, 0, 65535, seed=1)
+    assert e.value.code == z2.ENOMEM
+    S, Cb = 8, 9
+    ctx = z2.Context(0, S, Cb, 1024, 0, 0, seed=3)
+    lg = np.random.default_rng(3).normal(0, 3, (S, Cb, 1024)).astype(np.float32)
+    codes = torch.full((S, Cb), -7, dtype=torch.int32, device=cuda)
+    p = z2.SampleParams(0.7, 50, 0.9, 0.02, 1.0, 1023)
+    ctx.sample(_t(lg, cuda), p, codes)
+    torch.cuda.synchronize()
+    rng = oracle.rng_seed_streams(3, S)
+    oc, _, _ = oracle.step(lg, make_params(0.7, 50, 0.9, 0.02, 1.0, 1023), rng, None, exp_mode=1)
+    assert (codes.cpu().numpy() == oc).all()
+    assert (ctx.get_rng() == rng).all()
+    ctx.close()

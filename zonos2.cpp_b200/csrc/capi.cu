@@ -36,6 +36,11 @@ namespace {
 int cuda_fail(cudaError_t e, const char *what)
 {
     snprintf(tl_error, sizeof(tl_error), "%s: %s", what, cudaGetErrorString(e));
+    // A failed call (cudaMalloc out of memory, say) also leaves its error in the
+    // thread's last-error slot, where the next launch's cudaGetLastError would
+    // find it and fail an unrelated call: the error is reported here, so clear it
+    // (a sticky error stays in the context regardless).
+    (void)cudaGetLastError();
     return e == cudaErrorMemoryAllocation ? ZONOS2CU_ENOMEM : ZONOS2CU_ECUDA;
 }
 

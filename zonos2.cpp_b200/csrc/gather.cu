@@ -17,7 +17,10 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <chrono>
 #include <mutex>
+#include <set>
+#include <thread>
 
 #include "zonos2_cuda.h"
 
@@ -39,6 +42,13 @@ struct NcclApi {
     ncclResult_t (*GroupStart)() = nullptr;
     ncclResult_t (*GroupEnd)() = nullptr;
     const char *(*GetErrorString)(ncclResult_t) = nullptr;
+    // Non-blocking set-up and tear-down (NCCL >= 2.14); the bounded calls need them.
+    bool nb_ok = false;
+    ncclResult_t (*CommInitRankConfig)(ncclComm_t *, int, ncclUniqueId, int,
+                                       ncclConfig_t *) = nullptr;
+    ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t *) = nullptr;
+    ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommFinalize)(ncclComm_t) = nullptr;
 };
 std::mutex g_nccl_mu;
 NcclApi g_nccl;
@@ -69,6 +79,9 @@ const NcclApi *nccl()
            sym(h, "ncclRecv", &a.Recv) && sym(h, "ncclGroupStart", &a.GroupStart) &&
            sym(h, "ncclGroupEnd", &a.GroupEnd) && sym(h, "ncclGetErrorString", &a.GetErrorString);
     if (!a.ok) z2_set_error("%s: %s", "libnccl.so.2", "an entry point is missing");
+    a.nb_ok = sym(h, "ncclCommInitRankConfig", &a.CommInitRankConfig) &&
+              sym(h, "ncclCommGetAsyncError", &a.CommGetAsyncError) &&
+              sym(h, "ncclCommAbort", &a.CommAbort) && sym(h, "ncclCommFinalize", &a.CommFinalize);
     return a.ok ? &a : nullptr;
 }
 
@@ -96,6 +109,58 @@ struct DeviceScope {
         if (prev >= 0) cudaSetDevice(prev);
     }
 };
+
+// Communicators made non-blocking by zonos2cu_comm_create_timeout: their groups
+// and their tear-down complete in the background and are polled.
+std::set<void *> g_nonblocking;
+
+bool is_nonblocking(void *c)
+{
+    std::lock_guard<std::mutex> lk(g_nccl_mu);
+    return g_nonblocking.count(c) != 0;
+}
+
+void forget_comm(void *c)
+{
+    std::lock_guard<std::mutex> lk(g_nccl_mu);
+    g_nonblocking.erase(c);
+}
+
+// Polls a non-blocking communicator until its pending operation (set-up, a
+// group, finalisation) ends or timeout_ms passes.  Returns ncclSuccess, the
+// error the operation ended with, or ncclInProgress when the time ran out.
+ncclResult_t wait_async(const NcclApi *a, ncclComm_t c, int timeout_ms)
+{
+    using clk = std::chrono::steady_clock;
+    const clk::time_point deadline = clk::now() + std::chrono::milliseconds(timeout_ms);
+    for (;;) {
+        ncclResult_t st = ncclInProgress;
+        const ncclResult_t r = a->CommGetAsyncError(c, &st);
+        if (r != ncclSuccess) return r;
+        if (st != ncclInProgress) return st;
+        if (clk::now() >= deadline) return ncclInProgress;
+        std::this_thread::sleep_for(std::chrono::microseconds(200));
+    }
+}
+
+// A non-blocking communicator's grouped sends and receives may still be
+// connecting when ncclGroupEnd returns: how long the gather waits for them.
+constexpr int kGroupTimeoutMs = 120000;
+// ... and how long zonos2cu_comm_destroy waits for the flush before it aborts.
+constexpr int kFinalizeTimeoutMs = 60000;
+
+// The outcome of an enqueueing call (ncclSend, ncclGroupEnd): on a non-blocking
+// communicator ncclInProgress means it is still connecting to its peers, and is
+// polled up to kGroupTimeoutMs.
+int settle(const NcclApi *a, ncclComm_t c, ncclResult_t r, const char *what)
+{
+    if (r == ncclInProgress && is_nonblocking(c)) r = wait_async(a, c, kGroupTimeoutMs);
+    if (r == ncclInProgress) {
+        z2_set_error("%s: %s", what, "not enqueued within the timeout");
+        return ZONOS2CU_ENCCL;
+    }
+    return r == ncclSuccess ? ZONOS2CU_OK : nccl_fail(a, r, what);
+}
 
 }  // namespace
 
@@ -143,12 +208,80 @@ int zonos2cu_comm_create(int device, int n_ranks, int rank, const unsigned char 
     return ZONOS2CU_OK;
 }
 
+int zonos2cu_comm_create_timeout(int device, int n_ranks, int rank, const unsigned char id[128],
+                                 int timeout_ms, void **comm_out)
+{
+    if (!id || !comm_out || n_ranks < 1 || rank < 0 || rank >= n_ranks || timeout_ms < 1)
+        return ZONOS2CU_EINVAL;
+    *comm_out = nullptr;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev)
+        return ZONOS2CU_EINVAL;
+    const NcclApi *a = nccl();
+    if (!a) return ZONOS2CU_ENCCL;
+    if (!a->nb_ok) {
+        z2_set_error("%s: %s", "libnccl.so.2", "no non-blocking communicator set-up");
+        return ZONOS2CU_ENCCL;
+    }
+    DeviceScope g(device);
+    ncclUniqueId u;
+    memcpy(u.internal, id, 128);
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    ncclComm_t c = nullptr;
+    ncclResult_t r = a->CommInitRankConfig(&c, n_ranks, u, rank, &cfg);
+    if ((r == ncclSuccess || r == ncclInProgress) && c) r = wait_async(a, c, timeout_ms);
+    if (r != ncclSuccess) {
+        if (c) a->CommAbort(c);   // also ends the set-up still waiting for its peers
+        if (r == ncclInProgress) {
+            z2_set_error("%s: %s", "ncclCommInitRankConfig",
+                         "not every rank joined within the timeout; aborted");
+            return ZONOS2CU_ENCCL;
+        }
+        return nccl_fail(a, r, "ncclCommInitRankConfig");
+    }
+    {
+        std::lock_guard<std::mutex> lk(g_nccl_mu);
+        g_nonblocking.insert(c);
+    }
+    *comm_out = c;
+    return ZONOS2CU_OK;
+}
+
 int zonos2cu_comm_destroy(void *comm)
 {
     if (!comm) return ZONOS2CU_OK;
     const NcclApi *a = nccl();
     if (!a) return ZONOS2CU_ENCCL;
-    Z2_NCCL(a, a->CommDestroy(static_cast<ncclComm_t>(comm)));
+    const ncclComm_t c = static_cast<ncclComm_t>(comm);
+    if (is_nonblocking(comm)) {
+        forget_comm(comm);
+        ncclResult_t r = a->CommFinalize(c);
+        if (r == ncclSuccess || r == ncclInProgress) r = wait_async(a, c, kFinalizeTimeoutMs);
+        if (r != ncclSuccess) {
+            a->CommAbort(c);
+            if (r == ncclInProgress) {
+                z2_set_error("%s: %s", "ncclCommFinalize", "did not flush within the timeout; aborted");
+                return ZONOS2CU_ENCCL;
+            }
+            return nccl_fail(a, r, "ncclCommFinalize");
+        }
+    }
+    Z2_NCCL(a, a->CommDestroy(c));
+    return ZONOS2CU_OK;
+}
+
+int zonos2cu_comm_abort(void *comm)
+{
+    if (!comm) return ZONOS2CU_OK;
+    const NcclApi *a = nccl();
+    if (!a) return ZONOS2CU_ENCCL;
+    if (!a->nb_ok) {
+        z2_set_error("%s: %s", "libnccl.so.2", "ncclCommAbort is missing");
+        return ZONOS2CU_ENCCL;
+    }
+    forget_comm(comm);
+    Z2_NCCL(a, a->CommAbort(static_cast<ncclComm_t>(comm)));
     return ZONOS2CU_OK;
 }
 
@@ -171,8 +304,8 @@ int zonos2cu_gather_codes(void *comm, int root, const int32_t *codes_dev, int n_
     if (n_steps == 0 || n_streams == 0) return ZONOS2CU_OK;
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (rank != root) {
-        if (my_elems) Z2_NCCL(a, a->Send(codes_dev, my_elems, ncclInt32, root, c, st));
-        return ZONOS2CU_OK;
+        if (!my_elems) return ZONOS2CU_OK;
+        return settle(a, c, a->Send(codes_dev, my_elems, ncclInt32, root, c, st), "ncclSend");
     }
     // the root: every other rank's block in rank order, its own copied in place
     Z2_NCCL(a, a->GroupStart());
@@ -188,13 +321,14 @@ int zonos2cu_gather_codes(void *comm, int root, const int32_t *codes_dev, int n_
             return nccl_fail(a, res, "ncclRecv");
         }
     }
-    Z2_NCCL(a, a->GroupEnd());
+    if (const int rc = settle(a, c, a->GroupEnd(), "ncclGroupEnd")) return rc;
     int32_t *mine = out_dev + (size_t)n_steps * (size_t)first * (size_t)n_cb;
     if (my_elems && mine != codes_dev) {
         const cudaError_t e = cudaMemcpyAsync(mine, codes_dev, sizeof(int32_t) * my_elems,
                                               cudaMemcpyDeviceToDevice, st);
         if (e != cudaSuccess) {
             z2_set_error("%s: %s", "root block copy", cudaGetErrorString(e));
+            (void)cudaGetLastError();   // reported here: not left for the next launch
             return ZONOS2CU_ECUDA;
         }
     }

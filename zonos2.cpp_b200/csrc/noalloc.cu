@@ -68,12 +68,18 @@ CUcontext current_context()
 int scratch_in_current_context(cudaStream_t stream, float **out)
 {
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-    if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) return ZONOS2CU_ECUDA;
+    if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) {
+        (void)cudaGetLastError();   // reported here: not left for the next launch
+        return ZONOS2CU_ECUDA;
+    }
     std::lock_guard<std::mutex> lock(g_addr.mu);
     const CUcontext ctx = current_context();
     if (cap == cudaStreamCaptureStatusNone) {
         void *p = nullptr;
-        if (cudaGetSymbolAddress(&p, g_noalloc_logits) != cudaSuccess || !p) return ZONOS2CU_ECUDA;
+        if (cudaGetSymbolAddress(&p, g_noalloc_logits) != cudaSuccess || !p) {
+            (void)cudaGetLastError();
+            return ZONOS2CU_ECUDA;
+        }
         *out = static_cast<float *>(p);
         if (!ctx) return ZONOS2CU_OK;
         int i = 0;   // record it, most recent first

@@ -43,7 +43,7 @@ EXPORTS = (
     "zonos2cu_gen_shear_up", "zonos2cu_set_embeddings", "zonos2cu_gen_embed_next",
     "zonos2cu_embed_frames", "zonos2cu_write_codes_bin", "zonos2cu_shard_range",
     "zonos2cu_comm_unique_id", "zonos2cu_comm_create", "zonos2cu_comm_destroy",
-    "zonos2cu_gather_codes",
+    "zonos2cu_gather_codes", "zonos2cu_comm_create_timeout", "zonos2cu_comm_abort",
 )
 
 
@@ -128,6 +128,8 @@ def lib() -> C.CDLL:
         "zonos2cu_comm_unique_id": (i, [C.c_char_p]),
         "zonos2cu_comm_create": (i, [i, i, i, C.c_char_p, C.POINTER(vp)]),
         "zonos2cu_comm_destroy": (i, [vp]),
+        "zonos2cu_comm_create_timeout": (i, [i, i, i, C.c_char_p, i, C.POINTER(vp)]),
+        "zonos2cu_comm_abort": (i, [vp]),
         "zonos2cu_gather_codes": (i, [vp, i, vp, i, ll, i, vp, vp]),
     }
     for name, (res, args) in sig.items():
@@ -253,12 +255,19 @@ class Comm:
     """An NCCL communicator made by the library (zonos2cu_comm_create); every
     rank creates it collectively with the id rank 0 made."""
 
-    def __init__(self, device: int, n_ranks: int, rank: int, uid: bytes):
+    def __init__(self, device: int, n_ranks: int, rank: int, uid: bytes,
+                 timeout_ms: int | None = None):
+        """timeout_ms: set up without blocking and abort if not every rank joins
+        in time (zonos2cu_comm_create_timeout); None: NCCL's blocking set-up."""
         if len(uid) != 128:
             raise ValueError("an NCCL unique id is 128 bytes")
         h = C.c_void_p()
-        _check(lib().zonos2cu_comm_create(device, n_ranks, rank, uid, C.byref(h)),
-               "zonos2cu_comm_create")
+        if timeout_ms is None:
+            _check(lib().zonos2cu_comm_create(device, n_ranks, rank, uid, C.byref(h)),
+                   "zonos2cu_comm_create")
+        else:
+            _check(lib().zonos2cu_comm_create_timeout(device, n_ranks, rank, uid, timeout_ms,
+                                                      C.byref(h)), "zonos2cu_comm_create_timeout")
         self.h, self.n_ranks, self.rank = h, n_ranks, rank
 
     def gather_codes(self, root: int, codes, n_steps: int, n_streams: int, n_cb: int, out=None,
@@ -269,8 +278,13 @@ class Comm:
 
     def close(self) -> None:
         if self.h:
-            _check(lib().zonos2cu_comm_destroy(self.h), "zonos2cu_comm_destroy")
-            self.h = C.c_void_p()
+            h, self.h = self.h, C.c_void_p()
+            _check(lib().zonos2cu_comm_destroy(h), "zonos2cu_comm_destroy")
+
+    def abort(self) -> None:
+        if self.h:
+            h, self.h = self.h, C.c_void_p()
+            _check(lib().zonos2cu_comm_abort(h), "zonos2cu_comm_abort")
 
 
 def device_error() -> int:
