@@ -22,8 +22,8 @@
  *         owned by the context);
  *       the first zonos2cu_sample_token on a device (a small per-device
  *         staging area, device and page-locked host memory, kept until exit);
- *       zonos2cu_comm_create (NCCL's own buffers, freed by
- *         zonos2cu_comm_destroy).
+ *       zonos2cu_comm_create and zonos2cu_comm_create_timeout (NCCL's own
+ *         buffers, freed by zonos2cu_comm_destroy or zonos2cu_comm_abort).
  *     Every other entry point, zonos2cu_step_noalloc included, allocates
  *     nothing.
  *   - Host buffers given to the "_host" calls are copied with
