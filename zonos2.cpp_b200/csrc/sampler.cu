@@ -1197,8 +1197,9 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
         float mx = -INFINITY;
         uint32_t km = allowm & validm;   // slots that keep their logit
         bool nonfin = false;
+        float w;   // the row max, or NaN: the careful form
         {
-            float acc = 1.0f;
+            float acc = __int_as_float(0x7fc00000);   // NaN: a penalty below 1 takes the careful form
             if (a.rho >= 1.0f) {   // slots in pairs: the products and the fma packed (f32x2)
                 float2 acc2 = make_float2(0.0f, 0.0f);
                 const float2 ir2 = make_float2(a.inv_rho, a.inv_rho);
@@ -1217,15 +1218,24 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
                 }
                 acc = __fadd_rn(acc2.x, acc2.y);
             }
-            if (__any_sync(kFull, !(acc == 0.0f)))
-                mx = careful_prologue(rowf, lane, V, seenm, allowm, validm, a.rho, a.inv_rho, v,
-                                      &km, &nonfin);
+            // acc is 0, or NaN if a slot of this lane is non-finite, so mx + acc is the
+            // lane's max or NaN, and the warp's NaN-propagating max (one instruction,
+            // sm_100a; a max, so exact) is the row max or NaN.  The test needs no vote
+            // of its own (0.0678 against 0.0682 ms); -0 + 0 = +0 changes no logit
+            // difference, so no token.
+            asm("redux.sync.max.NaN.f32 %0, %1, 0xffffffff;" : "=f"(w) : "f"(__fadd_rn(mx, acc)));
         }
-        // the warp's max in one instruction (sm_100a; a max, so exact); mx is never
-        // NaN here (non-finite rows took the careful prologue)
-        asm("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(mx) : "f"(mx));
+        int nf_flag = 0;
+        if (isnan(w)) {   // the careful form, and the non-finite flag only it can raise
+            mx = careful_prologue(rowf, lane, V, seenm, allowm, validm, a.rho, a.inv_rho, v, &km,
+                                  &nonfin);
+            asm("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(mx) : "f"(mx));
+            nf_flag = __any_sync(kFull, nonfin) ? 2 : 0;
+        } else {
+            mx = w;
+        }
         const bool live = mx >= -1e9f;  // running max starts at -1e9: :41-42
-        const int flag = (__any_sync(kFull, nonfin) ? 2 : 0) | (live ? 0 : 1);
+        const int flag = nf_flag | (live ? 0 : 1);
         // The evicted token leaves the history index now that the row's set has been
         // read: its count drops (two u16 counts per word); the old count comes back
         // by the end of the row.
@@ -1381,7 +1391,8 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
                         const uint32_t q = gap_q15(rowf[t], s126, Ms126, &b8);
                         int pos = kRegSortMax;
                         if (has) pos = (int)atomicAdd(hist + b8, 1u);
-                        stage[pos] = ~((q << 10) | (uint32_t)t);
+                        // ~(q << 10 | t) as one multiply-add on the fma pipe (t < 1024)
+                        stage[pos] = q * (uint32_t)-1024 + ~(uint32_t)t;
                     }
                 }
                 __syncwarp();
@@ -1415,7 +1426,9 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
                 for (int e = 0; e < 4; e++) {
                     tk[e] = ~ck[e] & 1023u;
                     lv[e] = rowf[tk[e]];
-                    pv[e] = 4 * lane + e < n_c ? ex2_approx(__fmul_rn(__fsub_rn(lv[e], M), c2)) : 0.0f;
+                    // positions past n_c hold key 0 (token 1023: a logit <= M or -inf, so
+                    // pv in [0, 1]); every use of pv is limited to n_c, m or mm positions
+                    pv[e] = ex2_approx(__fmul_rn(__fsub_rn(lv[e], M), c2));
                 }
                 __syncwarp();   // the row and the stage are free
                 if (cb_nx < NCB) issue(s_nx, cb_nx);
