@@ -172,15 +172,9 @@ __device__ __forceinline__ float prologue(float x, int i, uint32_t seenm, uint32
 // s = 1 / (126 * width), and the bucket is round(126 u), read from the low byte
 // of 126 u + 2^23 (the histogram does this two slots at a time); -inf and gaps
 // past 126 widths land in 126, the open-ended last bucket.  The saturating fma
-// clamps on the fma pipe.  gap_q15 is the same coordinate 126 u + 1/2 rounded
-// to a multiple of 2^-15: an integer below 2^22, monotone non-increasing in v.
-__device__ __forceinline__ uint32_t gap_q15(float v, float s126, float Ms126, uint32_t *bucket)
-{
-    float u;
-    asm("fma.rn.sat.f32 %0, %1, %2, %3;" : "=f"(u) : "f"(-v), "f"(s126), "f"(Ms126));
-    *bucket = __float_as_uint(__fmaf_rn(u, 126.0f, 0x1p23f)) & 0xffu;   // as the histogram's
-    return __float_as_uint(__fmaf_rn(u, 126.0f * 32768.0f, 16384.0f + 0x1p23f)) - 0x4B000000u;
-}
+// clamps on the fma pipe.  The scatter's sort key carries the same coordinate
+// 126 u + 1/2 rounded to a multiple of 2^-15 (an integer below 2^22, monotone
+// non-increasing in v) and recomputes the bucket bit for bit.
 
 // a * b + c on both halves, each saturated to [0, 1] (the packed f32x2 fma has
 // no saturating form, so two scalar ones: still the fma pipe, not the ALU's)
@@ -1387,12 +1381,26 @@ __global__ void __launch_bounds__(32 * kWarps, kCtasPerSm) sample_rows_kernel(co
                         const int i = __ffs(sm | 0x80000000u) - 1;
                         sm &= sm - 1u;
                         const int t = slot_token(lane, i);
-                        uint32_t b8;
-                        const uint32_t q = gap_q15(rowf[t], s126, Ms126, &b8);
+                        // the gap coordinate on the raw float bits: the bucket bits
+                        // 0x4B000000 + b (as the histogram's) address the counter as
+                        // bits * 4 + hbase, and q = qbits - 0x4B000000 enters the key
+                        // ~(q << 10 | t) = q * -1024 + ~t (t < 1024) as qbits, since
+                        // 0x4B000000 * 1024 = 0 mod 2^32: one multiply-add each
+                        float gu;
+                        asm("fma.rn.sat.f32 %0, %1, %2, %3;" : "=f"(gu) : "f"(-rowf[t]), "f"(s126), "f"(Ms126));
+                        const uint32_t bbits = __float_as_uint(__fmaf_rn(gu, 126.0f, 0x1p23f));
+                        const uint32_t qbits =
+                            __float_as_uint(__fmaf_rn(gu, 126.0f * 32768.0f, 16384.0f + 0x1p23f));
                         int pos = kRegSortMax;
-                        if (has) pos = (int)atomicAdd(hist + b8, 1u);
-                        // ~(q << 10 | t) as one multiply-add on the fma pipe (t < 1024)
-                        stage[pos] = q * (uint32_t)-1024 + ~(uint32_t)t;
+                        if (has) {
+                            uint32_t old;
+                            asm volatile("atom.shared.add.u32 %0, [%1], 1;"
+                                         : "=r"(old)
+                                         : "r"(bbits * 4u + hbase)
+                                         : "memory");
+                            pos = (int)old;
+                        }
+                        stage[pos] = qbits * (uint32_t)-1024 + ~(uint32_t)t;
                     }
                 }
                 __syncwarp();
