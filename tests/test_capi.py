@@ -146,3 +146,10 @@ def test_gather_and_comm_reject_bad_arguments(z2):
     assert L.zonos2cu_comm_create(0, 2, 2, uid, C.byref(h)) == z2.EINVAL
     assert L.zonos2cu_comm_create(0, 1, 0, None, C.byref(h)) == z2.EINVAL
     assert L.zonos2cu_comm_destroy(None) == 0
+    # the bounded set-up: the same checks, and a timeout of at least 1 ms
+    assert L.zonos2cu_comm_create_timeout(0, 0, 0, uid, 1000, C.byref(h)) == z2.EINVAL
+    assert L.zonos2cu_comm_create_timeout(0, 2, 2, uid, 1000, C.byref(h)) == z2.EINVAL
+    assert L.zonos2cu_comm_create_timeout(0, 1, 0, None, 1000, C.byref(h)) == z2.EINVAL
+    assert L.zonos2cu_comm_create_timeout(0, 1, 0, uid, 0, C.byref(h)) == z2.EINVAL
+    assert L.zonos2cu_comm_create_timeout(0, 1, 0, uid, -5, C.byref(h)) == z2.EINVAL
+    assert L.zonos2cu_comm_abort(None) == 0
