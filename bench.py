@@ -73,9 +73,9 @@ FUSED_ROW_BYTES = 4 * VOCAB + 4 * HIST + 8        # no allow bits in the fused c
 DESIGN_ROW_BYTES = 4 * VOCAB + 128 + 8 + 8 + 8 + 128 / NCB + 64 / NCB
 # DRAM bytes (read + write) of one sample_rows_kernel launch on this workload,
 # from an ncu capture of `bench.py --steps 12 --warmup 3 --no-cpu-baseline
-# --no-head --no-fused`, launch 11 (dram__bytes_read.sum 167.20 MB +
-# dram__bytes_write.sum 7.25 MB).
-SAMPLER_TRAFFIC_BYTES = 174.45e6
+# --no-head --no-fused`, launch 11 (dram__bytes_read.sum 167.11 MB +
+# dram__bytes_write.sum 5.60 MB).
+SAMPLER_TRAFFIC_BYTES = 172.70e6
 # Kernels of ours per decode step: the persistent sampler (the decode context
 # draws each step's uniforms during the step before).
 LAUNCHES_PER_STEP = 1
