@@ -9,8 +9,11 @@ top-k 100, top-p 0.9, min-p 0.02, T 0.7, repetition penalty 1.1 over a
 1024-entry history per row.  A step samples one batch of logits for every
 stream; the delay step cycles through a 128-step rollout.  Streams are
 batch-sharded: each of N ranks owns 4096 streams (weak scaling) and the int32
-codes are collected on rank 0 through the library's NCCL gather
-(zonos2cu_gather_codes) every 32 steps and after the last (every step in e2e).
+codes are collected on rank 0: in the device-resident loops every 32 steps (and
+after the last) a ring half is pushed into rank 0's buffer by the copy engines
+while the other half fills (zonos2cu_ipc_alloc / _ipc_open / _push_codes), in the
+end-to-end loop and the check through the library's NCCL gather
+(zonos2cu_gather_codes).
 Logits and history (151 MB each per rank) exceed the 126 MB L2, so no flush is
 needed between steps.
 
@@ -22,7 +25,7 @@ measured HBM copy bandwidth, ``cpu_baseline`` (the reference's own
 sample_token, compiled unmodified, timed on this host), ``fused`` (the
 batch-sharded fused configuration: bf16 head GEMM + softcap + sampler over 4096
 streams per rank, at every N), ``multi_gpu_check`` (N > 1: rank 0's gathered
-codes against a one-GPU context over the whole global batch), ``clocks``
+and pushed codes against a one-GPU context over the whole global batch), ``clocks``
 sampled through NVML during the timed regions, and ``gpu_launches``.
 
 ``--impl reference`` times the reference's CPU implementation of the same
@@ -52,7 +55,7 @@ METRIC = "sampled codes/sec (streams×9 codebooks) at B=4096; % HBM roofline; 1/
 STREAMS, NCB, VOCAB, HIST, DIM = 4096, 9, 1024, 1024, 2048
 TOPK, TOPP, MINP, TEMP, RHO, PAD = 100, 0.9, 0.02, 0.7, 1.1, 1023
 ROLLOUT = 128
-GATHER_EVERY = 32  # device-resident loops: steps of codes per gather to rank 0
+GATHER_EVERY = 32  # device-resident loops: steps of codes per push to rank 0
 VERIFY_STEPS = 3   # N > 1: steps compared against a one-GPU run of the global batch
 WORKLOAD = ("constrained sampling, 4096 streams x 9 codebooks x 1024 vocab per GPU: f32 "
             "logits ~N(0,4^2), 1% +8 spikes, softcap 15; delay masks over a 128-step rollout; "
@@ -322,7 +325,8 @@ def run_head_only(args):
 class Job:
     """One rank's view of the batch-sharded job: torch.distributed for the
     host-side plumbing (barriers, the timing max), the library's own NCCL
-    communicator for the codes gather to rank 0."""
+    communicator for the codes gather to rank 0, and rank 0's push buffer for
+    the copy-engine collection (zonos2cu_ipc_alloc / _ipc_open / _push_codes)."""
 
     def __init__(self, torch, Z):
         import torch.distributed as dist
@@ -339,6 +343,22 @@ class Job:
             box = [Z.comm_unique_id() if self.rank == 0 else None]
             dist.broadcast_object_list(box, src=0)
             self.comm = Z.Comm(self.local, self.ws, self.rank, box[0])
+            # rank 0's push buffer, [GATHER_EVERY][global streams][NCB] int32, mapped
+            # into every other rank; each rank's block of a step is contiguous
+            self.first, self.count = Z.shard_range(self.ws * STREAMS, self.ws, self.rank)
+            self.push_buf = None
+            box = [None]
+            if self.rank == 0:
+                self.push_buf, box[0] = Z.ipc_alloc(self.local,
+                                                    4 * GATHER_EVERY * self.ws * STREAMS * NCB)
+            dist.broadcast_object_list(box, src=0)
+            self.push_dst = self.push_buf if self.rank == 0 else Z.ipc_open(self.local, box[0])
+            self.copy_stream = torch.cuda.Stream(device=self.dev)
+            # the loops' rings have two halves of GATHER_EVERY steps: one is pushed
+            # while the other fills
+            self.ready = [torch.cuda.Event() for _ in range(2)]
+            self.done = [torch.cuda.Event() for _ in range(2)]
+            self.pushed = [False, False]
 
     def barrier(self):
         if self.ws > 1:
@@ -361,6 +381,34 @@ class Job:
         self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
         return tuple(float(x) for x in t.tolist())
 
+    def half_free(self, half):
+        """The step stream waits for the ring half's previous push before the half
+        is written again (once per GATHER_EVERY steps: a wait between two launches
+        cuts their programmatic overlap)."""
+        if self.ws > 1 and self.pushed[half]:
+            self.stream.wait_event(self.done[half])
+
+    def push_block(self, block, n_steps, half):
+        """This rank's codes of n_steps steps ([n_steps][count][NCB], ring half
+        `half`) to their place in rank 0's push buffer: one strided copy-engine
+        copy on the copy stream, ordered after those steps."""
+        if self.ws == 1:
+            return
+        self.ready[half].record(self.stream)
+        self.copy_stream.wait_event(self.ready[half])
+        self.Z.push_codes(block, n_steps, self.count * NCB, self.push_dst + 4 * self.first * NCB,
+                          self.ws * STREAMS * NCB, stream=self.copy_stream)
+        self.done[half].record(self.copy_stream)
+        self.pushed[half] = True
+
+    def pushes_done(self):
+        """The step stream waits for every push issued so far (inside a timed
+        region: the codes are on rank 0 when its end event fires)."""
+        if self.ws > 1:
+            ev = self.torch.cuda.Event()
+            ev.record(self.copy_stream)
+            self.stream.wait_event(ev)
+
     def gather(self, ring, n_steps, out):
         """n_steps of this rank's codes [n_steps][STREAMS][NCB] to rank 0."""
         if self.ws > 1 and n_steps > 0:
@@ -372,6 +420,11 @@ class Job:
             self.torch.cuda.synchronize()
             self.comm.close()
         if self.ws > 1:
+            if self.rank != 0:
+                self.Z.ipc_close(self.push_dst)
+            self.dist.barrier()   # every mapping closed before rank 0 frees the buffer
+            if self.rank == 0:
+                self.Z.ipc_free(self.push_buf)
             self.dist.barrier()
             self.dist.destroy_process_group()
 
@@ -398,7 +451,10 @@ def multi_gpu_check(job, params):
     if rank == 0:
         out = torch.zeros((ws * VERIFY_STEPS * STREAMS * NCB,), dtype=torch.int32, device=job.dev)
     job.gather(ring, VERIFY_STEPS, out)
-    job.torch.cuda.synchronize()
+    job.half_free(0)   # and the same steps pushed by the copy engines
+    job.push_block(ring, VERIFY_STEPS, 0)
+    job.pushes_done()
+    job.barrier()   # every rank's pushes complete before rank 0 reads its buffer
     ctx.close()
     del batches
     result = None
@@ -406,6 +462,12 @@ def multi_gpu_check(job, params):
         got = out.view(ws, VERIFY_STEPS, STREAMS, NCB).permute(1, 0, 2, 3).reshape(
             VERIFY_STEPS, ws * STREAMS, NCB).cpu().numpy()
         N = ws * STREAMS
+        pushed = torch.empty((VERIFY_STEPS * N * NCB,), dtype=torch.int32, device=job.dev)
+        Z.push_codes(job.push_dst, 1, VERIFY_STEPS * N * NCB, pushed.data_ptr(),
+                     VERIFY_STEPS * N * NCB, stream=job.stream)
+        torch.cuda.synchronize()
+        got_push = pushed.view(VERIFY_STEPS, N, NCB).cpu().numpy()
+        del pushed
         whole = Z.Context(job.local, N, NCB, VOCAB, 0, HIST, seed=1234, first_stream=0)
         parts = [make_device_inputs(torch, job.dev, r) for r in range(ws)]
         whole.set_history(np.concatenate([p[1] for p in parts]), 0)
@@ -422,10 +484,13 @@ def multi_gpu_check(job, params):
         del glog
         mism = int((got != want).sum())
         result = {"steps": VERIFY_STEPS, "global_streams": N, "rows": int(want.size),
-                  "mismatches": mism, "sha256_16_gathered": codes_digest(got),
+                  "mismatches": mism, "mismatches_pushed": int((got_push != want).sum()),
+                  "sha256_16_gathered": codes_digest(got),
+                  "sha256_16_pushed": codes_digest(got_push),
                   "sha256_16_one_gpu": codes_digest(want),
-                  "what": "rank 0's gathered codes of the sharded run vs one context over the "
-                          "whole global batch on rank 0's GPU"}
+                  "what": "rank 0's codes of the sharded run, gathered over NCCL and pushed by "
+                          "the copy engines, vs one context over the whole global batch on "
+                          "rank 0's GPU"}
         torch.cuda.empty_cache()
     job.barrier()
     return result
@@ -440,22 +505,21 @@ def time_sampler(job, params, steps, warmup, clocks):
     ctx.set_history(hist, 0)
     ctx.set_allow(allow)
     flags = torch.zeros((STREAMS, NCB), dtype=torch.int32, device=job.dev)
-    ring = torch.zeros((GATHER_EVERY, STREAMS, NCB), dtype=torch.int32, device=job.dev)
-    out = None
-    if job.rank == 0 and job.ws > 1:
-        out = torch.zeros((job.ws * GATHER_EVERY * STREAMS * NCB,), dtype=torch.int32,
-                          device=job.dev)
+    ring = torch.zeros((2, GATHER_EVERY, STREAMS, NCB), dtype=torch.int32, device=job.dev)
 
     def run(t0, n):
-        filled = 0
+        # every GATHER_EVERY steps (and after the last) the filled ring half is
+        # pushed to rank 0 by the copy engines while the other half fills (N > 1)
         for i in range(n):
             t = t0 + i
-            ctx.sample(batches[t % 2], params, ring[i % GATHER_EVERY], flags,
+            blk, j = divmod(i, GATHER_EVERY)
+            if j == 0:
+                job.half_free(blk % 2)
+            ctx.sample(batches[t % 2], params, ring[blk % 2, j], flags,
                        delay_step=t % ROLLOUT, stream=job.stream)
-            filled += 1
-            if filled == GATHER_EVERY or i == n - 1:
-                job.gather(ring, filled, out)
-                filled = 0
+            if j == GATHER_EVERY - 1 or i == n - 1:
+                job.push_block(ring[blk % 2], j + 1, blk % 2)
+        job.pushes_done()
 
     run(0, warmup)
     job.barrier()
@@ -473,7 +537,7 @@ def time_sampler(job, params, steps, warmup, clocks):
     ke = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     for i in range(steps):
         ks[i].record(job.stream)
-        ctx.sample(batches[i % 2], params, ring[i % GATHER_EVERY], flags,
+        ctx.sample(batches[i % 2], params, ring[0, i % GATHER_EVERY], flags,
                    delay_step=(warmup + steps + i) % ROLLOUT, stream=job.stream)
         ke[i].record(job.stream)
     job.barrier()
@@ -538,9 +602,10 @@ def time_e2e(job, params, inputs, steps, clocks):
 
 def time_fused(job, steps, warmup, clocks):
     """The batch-sharded fused configuration: per rank 4096 streams, bf16
-    head GEMM + softcap + sampler per step (zonos2cu_ctx_step), codes to rank 0
-    every 32 steps.  Returns the timed region's ms and the head / sampler
-    kernel times from a second pass with events between the two kernels."""
+    head GEMM + softcap + sampler per step (zonos2cu_ctx_step), each step's
+    codes pushed to rank 0 by the copy engines.  Returns the timed region's ms
+    and the head / sampler kernel times from a second pass with events between
+    the two kernels."""
     torch, Z = job.torch, job.Z
     import workloads as W
     cfg = W.CONFIGS[5]
@@ -553,20 +618,17 @@ def time_fused(job, steps, warmup, clocks):
     g.manual_seed(cfg.seed + 7919 * job.rank)
     hidden = [torch.randn((count, DIM), generator=g, device=job.dev).to(torch.bfloat16)
               for _ in range(2)]
-    ring = torch.zeros((GATHER_EVERY, count, NCB), dtype=torch.int32, device=job.dev)
-    out = None
-    if job.rank == 0 and job.ws > 1:
-        out = torch.zeros((job.ws * GATHER_EVERY * STREAMS * NCB,), dtype=torch.int32,
-                          device=job.dev)
+    ring = torch.zeros((2, GATHER_EVERY, count, NCB), dtype=torch.int32, device=job.dev)
 
     def run(t0, n):
-        filled = 0
         for i in range(n):
-            ctx.step(hidden[(t0 + i) % 2], Z.BF16, p, ring[i % GATHER_EVERY], stream=job.stream)
-            filled += 1
-            if filled == GATHER_EVERY or i == n - 1:
-                job.gather(ring, filled, out)
-                filled = 0
+            blk, j = divmod(i, GATHER_EVERY)
+            if j == 0:
+                job.half_free(blk % 2)
+            ctx.step(hidden[(t0 + i) % 2], Z.BF16, p, ring[blk % 2, j], stream=job.stream)
+            if j == GATHER_EVERY - 1 or i == n - 1:
+                job.push_block(ring[blk % 2], j + 1, blk % 2)
+        job.pushes_done()
 
     run(0, warmup)
     job.barrier()
@@ -592,7 +654,7 @@ def time_fused(job, steps, warmup, clocks):
         ev[i][0].record(job.stream)
         Z.head_softcap(Wt, Z.BF16, VOCAB, NCB, VOCAB, hidden[i % 2], lg, stream=job.stream)
         ev[i][1].record(job.stream)
-        ctx.sample(lg, p, ring[i % GATHER_EVERY], stream=job.stream)
+        ctx.sample(lg, p, ring[0, i % GATHER_EVERY], stream=job.stream)
         ev[i][2].record(job.stream)
     job.barrier()
     head_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / n_ev
@@ -635,7 +697,8 @@ def run_ours(args):
             "workload": FUSED_WORKLOAD, "streams_per_gpu": STREAMS, "n_gpus": ws,
             "steps": args.steps, "ms_per_step": f_total / args.steps,
             "codes_per_s": rows * ws * args.steps / (f_total / 1e3),
-            "gather": f"codes to rank 0 every {GATHER_EVERY} steps and after the last",
+            "gather": f"codes pushed to rank 0 by the copy engines every {GATHER_EVERY} steps "
+                      f"and after the last",
             "sampler_ms_events": f_samp,
             "head_ms_events": head_ms,
             "head_tflops": flops / (head_ms / 1e3) / 1e12,
@@ -663,7 +726,7 @@ def run_ours(args):
     launch_bytes = ROW_BYTES * rows
     # The sampler's mean launch time: over the whole timed region at one GPU (it
     # holds nothing but the sampler's launches), from the per-launch events where
-    # the region also holds the gathers.
+    # the region also waits for the pushes to rank 0.
     kern_ms = total_ms / args.steps if ws == 1 else ev_ms
     achieved = launch_bytes / (kern_ms / 1e3) / 1e9
 
@@ -686,9 +749,11 @@ def run_ours(args):
         "data": "synthetic",
         "config": {"workload": WORKLOAD, "streams_per_gpu": STREAMS, "codebooks": NCB,
                    "vocab": VOCAB,
-                   "parallelism": f"batch-sharded x{ws}, codes gathered to rank 0 over NCCL "
-                                  f"(zonos2cu_gather_codes) every {GATHER_EVERY} steps and "
-                                  f"after the last (every step in e2e)",
+                   "parallelism": f"batch-sharded x{ws}, codes pushed to rank 0 by the copy "
+                                  f"engines every {GATHER_EVERY} steps and after the last "
+                                  f"(zonos2cu_push_codes into its zonos2cu_ipc_alloc buffer); "
+                                  f"end to end: gathered over NCCL (zonos2cu_gather_codes) "
+                                  f"every step",
                    "l2": "inputs larger than L2 (151 MB logits + 151 MB history per GPU per step)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": args.traffic,

@@ -23,7 +23,8 @@
  *       the first zonos2cu_sample_token on a device (a small per-device
  *         staging area, device and page-locked host memory, kept until exit);
  *       zonos2cu_comm_create and zonos2cu_comm_create_timeout (NCCL's own
- *         buffers, freed by zonos2cu_comm_destroy or zonos2cu_comm_abort).
+ *         buffers, freed by zonos2cu_comm_destroy or zonos2cu_comm_abort);
+ *       zonos2cu_ipc_alloc (freed by zonos2cu_ipc_free).
  *     Every other entry point, zonos2cu_step_noalloc included, allocates
  *     nothing.
  *   - Host buffers given to the "_host" calls are copied with
@@ -329,6 +330,33 @@ int zonos2cu_comm_abort(void *nccl_comm);
  * send and return. */
 int zonos2cu_gather_codes(void *nccl_comm, int root, const int32_t *codes_dev, int n_steps,
                           long long n_streams, int n_cb, int32_t *out_dev, void *stream);
+
+/* The same collection by the copy engines, for a loop that must not give SMs or
+ * a collective to it: the root allocates its output with zonos2cu_ipc_alloc
+ * (device memory of the library's own, freed by zonos2cu_ipc_free) and hands
+ * the 64-byte handle to every other rank out of band; each of those maps it
+ * once with zonos2cu_ipc_open (a pointer into the root's GPU, valid in this
+ * process until zonos2cu_ipc_close) and, after each block of steps, enqueues
+ * zonos2cu_push_codes of its codes to their place in the root's output, on a
+ * stream ordered after those steps.  The copies run on the copy engines over
+ * NVLink while the SMs run the next steps; no rank waits for another in the
+ * loop.  The caller orders the reuse of its source buffer after the copy (an
+ * event) and, before the root reads its output, the completion of every rank's
+ * copies (each rank synchronises its copy stream, then a barrier).  All on one
+ * node. */
+int zonos2cu_ipc_alloc(int device, long long bytes, void **dev_ptr_out, unsigned char handle[64]);
+int zonos2cu_ipc_free(void *dev_ptr);
+int zonos2cu_ipc_open(int device, const unsigned char handle[64], void **dev_ptr_out);
+int zonos2cu_ipc_close(void *dev_ptr);
+/* n_steps blocks of elems_per_step int32 codes, contiguous in codes_dev (e.g.
+ * [n_steps][count][n_cb] of a ring), to dst_dev + k * dst_stride for block k
+ * (e.g. rank r's place, first_r * n_cb, in the root's [n_steps][n_streams][n_cb]
+ * output: dst_stride = n_streams * n_cb), one strided copy asynchronous on
+ * `stream`.  Pushing a block of steps at a time keeps the step stream free of
+ * per-step event waits, which would cut the programmatic overlap of one step's
+ * launch with the step before. */
+int zonos2cu_push_codes(const int32_t *codes_dev, int n_steps, long long elems_per_step,
+                        int32_t *dst_dev, long long dst_stride, void *stream);
 
 /* ---- one decode step that allocates nothing -------------------------------- */
 

@@ -153,3 +153,24 @@ def test_gather_and_comm_reject_bad_arguments(z2):
     assert L.zonos2cu_comm_create_timeout(0, 1, 0, uid, 0, C.byref(h)) == z2.EINVAL
     assert L.zonos2cu_comm_create_timeout(0, 1, 0, uid, -5, C.byref(h)) == z2.EINVAL
     assert L.zonos2cu_comm_abort(None) == 0
+
+
+def test_push_gather_rejects_bad_arguments(z2):
+    """The copy-engine collection's checks come before CUDA is touched."""
+    L = z2.lib()
+    p = C.c_void_p()
+    hbuf = C.create_string_buffer(64)
+    assert L.zonos2cu_ipc_alloc(0, 1024, None, hbuf) == z2.EINVAL
+    assert L.zonos2cu_ipc_alloc(0, 1024, C.byref(p), None) == z2.EINVAL
+    assert L.zonos2cu_ipc_alloc(0, 0, C.byref(p), hbuf) == z2.EINVAL
+    assert L.zonos2cu_ipc_open(0, None, C.byref(p)) == z2.EINVAL
+    assert L.zonos2cu_ipc_open(0, bytes(64), None) == z2.EINVAL
+    assert L.zonos2cu_push_codes(None, -1, 9, None, 9, None) == z2.EINVAL
+    assert L.zonos2cu_push_codes(None, 1, -1, None, 9, None) == z2.EINVAL
+    assert L.zonos2cu_push_codes(1 << 20, 2, 9, 1 << 21, 8, None) == z2.EINVAL   # stride < block
+    assert L.zonos2cu_push_codes(None, 2, 9, 1 << 21, 9, None) == z2.EINVAL
+    assert L.zonos2cu_push_codes(1 << 20, 2, 9, None, 9, None) == z2.EINVAL
+    assert L.zonos2cu_push_codes(None, 0, 9, None, 9, None) == 0
+    assert L.zonos2cu_push_codes(None, 3, 0, None, 0, None) == 0
+    assert L.zonos2cu_ipc_free(None) == 0
+    assert L.zonos2cu_ipc_close(None) == 0

@@ -335,4 +335,110 @@ int zonos2cu_gather_codes(void *comm, int root, const int32_t *codes_dev, int n_
     return ZONOS2CU_OK;
 }
 
+
+// ---- codes pushed to one rank by copy engines ----------------------------------
+// The root's output lives in memory of its own (cudaMalloc: an IPC handle names a
+// whole allocation); every other rank maps it once (cudaIpcOpenMemHandle, peer
+// access enabled lazily) and after each step copies its block into it with
+// cudaMemcpyAsync on a stream of its own: the copy engines move it over NVLink
+// while the SMs run the next step, and no rank waits for another inside the loop.
+
+int zonos2cu_ipc_alloc(int device, long long bytes, void **dev_ptr_out, unsigned char handle[64])
+{
+    if (!dev_ptr_out || !handle || bytes <= 0) return ZONOS2CU_EINVAL;
+    *dev_ptr_out = nullptr;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) {
+        (void)cudaGetLastError();
+        return ZONOS2CU_EINVAL;
+    }
+    DeviceScope g(device);
+    void *p = nullptr;
+    cudaError_t e = cudaMalloc(&p, (size_t)bytes);
+    if (e != cudaSuccess) {
+        z2_set_error("%s: %s", "ipc buffer", cudaGetErrorString(e));
+        (void)cudaGetLastError();
+        return e == cudaErrorMemoryAllocation ? ZONOS2CU_ENOMEM : ZONOS2CU_ECUDA;
+    }
+    cudaIpcMemHandle_t h;
+    static_assert(sizeof(h) == 64, "CUDA IPC handle size");
+    e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        z2_set_error("%s: %s", "cudaIpcGetMemHandle", cudaGetErrorString(e));
+        (void)cudaGetLastError();
+        cudaFree(p);
+        return ZONOS2CU_ECUDA;
+    }
+    memcpy(handle, &h, 64);
+    *dev_ptr_out = p;
+    return ZONOS2CU_OK;
+}
+
+int zonos2cu_ipc_free(void *dev_ptr)
+{
+    if (!dev_ptr) return ZONOS2CU_OK;
+    const cudaError_t e = cudaFree(dev_ptr);
+    if (e != cudaSuccess) {
+        z2_set_error("%s: %s", "ipc buffer free", cudaGetErrorString(e));
+        (void)cudaGetLastError();
+        return ZONOS2CU_ECUDA;
+    }
+    return ZONOS2CU_OK;
+}
+
+int zonos2cu_ipc_open(int device, const unsigned char handle[64], void **dev_ptr_out)
+{
+    if (!handle || !dev_ptr_out) return ZONOS2CU_EINVAL;
+    *dev_ptr_out = nullptr;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) {
+        (void)cudaGetLastError();
+        return ZONOS2CU_EINVAL;
+    }
+    DeviceScope g(device);
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, 64);
+    void *p = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+        z2_set_error("%s: %s", "cudaIpcOpenMemHandle", cudaGetErrorString(e));
+        (void)cudaGetLastError();
+        return ZONOS2CU_ECUDA;
+    }
+    *dev_ptr_out = p;
+    return ZONOS2CU_OK;
+}
+
+int zonos2cu_ipc_close(void *dev_ptr)
+{
+    if (!dev_ptr) return ZONOS2CU_OK;
+    const cudaError_t e = cudaIpcCloseMemHandle(dev_ptr);
+    if (e != cudaSuccess) {
+        z2_set_error("%s: %s", "cudaIpcCloseMemHandle", cudaGetErrorString(e));
+        (void)cudaGetLastError();
+        return ZONOS2CU_ECUDA;
+    }
+    return ZONOS2CU_OK;
+}
+
+int zonos2cu_push_codes(const int32_t *codes_dev, int n_steps, long long elems_per_step,
+                        int32_t *dst_dev, long long dst_stride, void *stream)
+{
+    if (n_steps < 0 || elems_per_step < 0 || dst_stride < elems_per_step) return ZONOS2CU_EINVAL;
+    if (n_steps == 0 || elems_per_step == 0) return ZONOS2CU_OK;
+    if (!codes_dev || !dst_dev) return ZONOS2CU_EINVAL;
+    // n_steps blocks, contiguous at the source, dst_stride apart at the
+    // destination: one strided copy
+    const size_t w = sizeof(int32_t) * (size_t)elems_per_step;
+    const cudaError_t e = cudaMemcpy2DAsync(dst_dev, sizeof(int32_t) * (size_t)dst_stride, codes_dev,
+                                            w, w, (size_t)n_steps, cudaMemcpyDeviceToDevice,
+                                            static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) {
+        z2_set_error("%s: %s", "push copy", cudaGetErrorString(e));
+        (void)cudaGetLastError();
+        return ZONOS2CU_ECUDA;
+    }
+    return ZONOS2CU_OK;
+}
+
 }  // extern "C"

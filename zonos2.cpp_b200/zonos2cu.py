@@ -44,6 +44,8 @@ EXPORTS = (
     "zonos2cu_embed_frames", "zonos2cu_write_codes_bin", "zonos2cu_shard_range",
     "zonos2cu_comm_unique_id", "zonos2cu_comm_create", "zonos2cu_comm_destroy",
     "zonos2cu_gather_codes", "zonos2cu_comm_create_timeout", "zonos2cu_comm_abort",
+    "zonos2cu_ipc_alloc", "zonos2cu_ipc_free", "zonos2cu_ipc_open", "zonos2cu_ipc_close",
+    "zonos2cu_push_codes",
 )
 
 
@@ -131,6 +133,11 @@ def lib() -> C.CDLL:
         "zonos2cu_comm_create_timeout": (i, [i, i, i, C.c_char_p, i, C.POINTER(vp)]),
         "zonos2cu_comm_abort": (i, [vp]),
         "zonos2cu_gather_codes": (i, [vp, i, vp, i, ll, i, vp, vp]),
+        "zonos2cu_ipc_alloc": (i, [i, ll, C.POINTER(vp), C.c_char_p]),
+        "zonos2cu_ipc_free": (i, [vp]),
+        "zonos2cu_ipc_open": (i, [i, C.c_char_p, C.POINTER(vp)]),
+        "zonos2cu_ipc_close": (i, [vp]),
+        "zonos2cu_push_codes": (i, [vp, i, ll, vp, ll, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -285,6 +292,39 @@ class Comm:
         if self.h:
             h, self.h = self.h, C.c_void_p()
             _check(lib().zonos2cu_comm_abort(h), "zonos2cu_comm_abort")
+
+
+def ipc_alloc(device: int, nbytes: int):
+    """(device address, 64-byte handle) of a buffer other processes can map."""
+    p = C.c_void_p()
+    buf = C.create_string_buffer(64)
+    _check(lib().zonos2cu_ipc_alloc(device, nbytes, C.byref(p), buf), "zonos2cu_ipc_alloc")
+    return p.value, buf.raw
+
+
+def ipc_free(ptr: int) -> None:
+    _check(lib().zonos2cu_ipc_free(ptr), "zonos2cu_ipc_free")
+
+
+def ipc_open(device: int, handle: bytes) -> int:
+    """This process's address of another process's ipc_alloc buffer."""
+    if len(handle) != 64:
+        raise ValueError("a CUDA IPC handle is 64 bytes")
+    p = C.c_void_p()
+    _check(lib().zonos2cu_ipc_open(device, handle, C.byref(p)), "zonos2cu_ipc_open")
+    return p.value
+
+
+def ipc_close(ptr: int) -> None:
+    _check(lib().zonos2cu_ipc_close(ptr), "zonos2cu_ipc_close")
+
+
+def push_codes(codes, n_steps: int, elems_per_step: int, dst: int, dst_stride: int,
+               stream=None) -> None:
+    """n_steps contiguous blocks of elems_per_step int32 codes to dst + k * dst_stride
+    (elements; dst e.g. an ipc_open address) on `stream`."""
+    _check(lib().zonos2cu_push_codes(_ptr(codes), n_steps, elems_per_step, dst, dst_stride,
+                                     _stream(stream)), "zonos2cu_push_codes")
 
 
 def device_error() -> int:
